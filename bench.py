@@ -1,0 +1,397 @@
+"""Benchmark of the B200 triangle-attention path (BASELINE.json metric: tri-attn ms/layer & TFLOP/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 2|4|1|0]
+
+One step = the starting-node layer then the ending-node layer (the pair a pairformer block runs,
+pairformer.py:86-87), each with its residual add, on one batch of synthetic pair tensors:
+    z1 = z + TriAttStart(z);  z2 = z1 + TriAttEnd(z1)
+value = whole-job TFLOP/s with inputs resident in HBM (FLOPs per layer: 4 N^3 H C + 2 N^2 128 516 +
+2 N^2 128 128, the reference's convention, tools/prof/triatt_common.py:51).  e2e = the same metric through
+the C ABI with the pair tensor and mask copied host->device and the result device->host every step.
+
+--impl reference: the reference's CPU path (the fp32 restatement in oracle/, run on the host cores
+with all threads) on a bounded sample of attention rows of the same workload, extrapolated per layer.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, C, CZ, NPROJ = 4, 32, 128, 516
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+CONFIGS = {
+    0: dict(N=128, dtype="fp32", z_scale=1.0, pad="none", seed_z=0, seed_w=0, pair=False),
+    1: dict(N=384, dtype="fp16", z_scale=1.0, pad="fixed38", seed_z=1, seed_w=1, pair=True),
+    2: dict(N=1024, dtype="bf16", z_scale=0.5, pad="uniform15", seed_z=2, seed_w=2, pair=True),
+    4: dict(N=2048, dtype="bf16", z_scale=1.0, pad="frac05", seed_z=4, seed_w=4, pair=True),
+}
+
+
+def layer_flops(N: int, B: int = 1) -> dict:
+    core = 4 * B * N ** 3 * H * C
+    proj = 2 * B * N * N * CZ * NPROJ
+    out = 2 * B * N * N * CZ * H * C
+    return {"core": core, "proj": proj, "out": out, "total": core + proj + out}
+
+
+# ---- synthetic inputs (same recipe as the test oracle's make_inputs) ------------------------------
+def token_mask(N, pad, seed):
+    t = torch.ones(N)
+    if pad == "fixed38":
+        t[N - 38:] = 0
+    elif pad == "uniform15":
+        g = torch.Generator().manual_seed(10_000 + seed)
+        n_pad = int(torch.randint(0, int(0.15 * N) + 1, (1,), generator=g))
+        if n_pad:
+            t[N - n_pad:] = 0
+    elif pad == "frac05":
+        t[N - int(round(0.05 * N)):] = 0
+    return t
+
+
+def make_params(seed, gate_bias=1.0):
+    g = torch.Generator().manual_seed(seed)
+    std = (1.0 / CZ) ** 0.5
+    shapes = {"w_q": (128, 128), "w_k": (128, 128), "w_v": (128, 128), "w_g": (128, 128), "w_b": (4, 128),
+              "w_o": (128, 128)}
+    p = {k: torch.randn(s, generator=g) * std for k, s in shapes.items()}
+    p["ln_w"], p["ln_b"] = torch.ones(CZ), torch.zeros(CZ)
+    p["g_b"] = torch.full((128,), float(gate_bias))
+    return p
+
+
+def make_config_inputs(cfg_id: int, N: int | None = None, B: int = 1):
+    c = CONFIGS[cfg_id]
+    N = c["N"] if N is None else N
+    g = torch.Generator().manual_seed(c["seed_z"])
+    z = torch.randn((B, N, N, CZ), generator=g) * c["z_scale"]
+    t = token_mask(N, c["pad"], c["seed_z"])
+    pm = (t[:, None] * t[None, :]).expand(B, N, N).contiguous()
+    return z, pm, make_params(c["seed_w"]), make_params(c["seed_w"] + 100)
+
+
+# ---- clocks -------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi samples every 200 ms during the timed region (median SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx, self.rows, self.proc = gpu_index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except ValueError:
+            pass
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ---- distributed plumbing -------------------------------------------------------------------------
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---- CPU reference / baseline -----------------------------------------------------------------------
+def cpu_sample_seconds(cfg_id: int, rows: int, threads: int) -> tuple[float, int]:
+    """Seconds the CPU oracle (fp32, torch on the host cores) takes for `rows` attention rows of BOTH
+    layers of the pair, plus the per-layer fixed part (LN + tri bias of all rows)."""
+    from oracle.triattn_ref import tri_attention_ref  # CPU baseline leg only
+
+    torch.set_num_threads(threads)
+    z, pm, ps, pe = make_config_inputs(cfg_id)
+    t0 = time.perf_counter()
+    tri_attention_ref(z, pm, ps, starting=True, rows=(0, rows))
+    tri_attention_ref(z, pm, pe, starting=False, rows=(0, rows))
+    return time.perf_counter() - t0, z.shape[1]
+
+
+def cpu_pair_seconds(cfg_id: int, threads: int, budget_s: float = 12.0) -> tuple[float, str]:
+    """Per-pair CPU time, extrapolated from two bounded row samples (t = fixed + rows * per_row)."""
+    t1, N = cpu_sample_seconds(cfg_id, 1, threads)
+    r2 = max(2, min(N, int(budget_s / max(t1, 1e-3))))
+    t2, _ = cpu_sample_seconds(cfg_id, r2, threads)
+    per_row = max((t2 - t1) / (r2 - 1), 1e-9)
+    fixed = max(t1 - per_row, 0.0)
+    pair = fixed + per_row * N
+    return pair, f"{r2} of {N} attention rows per layer (start+end), fixed LN/tri-bias part timed, extrapolated"
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    N = cfg["N"]
+    threads = os.cpu_count() or 1
+    fl = layer_flops(N)["total"] * (2 if cfg["pair"] else 1)
+    from oracle.triattn_ref import tri_attention_ref  # the reference arm runs the CPU oracle by design
+
+    torch.set_num_threads(threads)
+    z, pm, ps, pe = make_config_inputs(args.config)
+    # size the per-step row sample so the whole run stays within a few minutes
+    t0 = time.perf_counter()
+    tri_attention_ref(z, pm, ps, starting=True, rows=(0, 1))
+    t_one = time.perf_counter() - t0
+    rows = max(1, min(N, int(6.0 / max(t_one, 1e-3))))
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        tri_attention_ref(z, pm, ps, starting=True, rows=(0, rows))
+        tri_attention_ref(z, pm, pe, starting=False, rows=(0, rows))
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+    step_s = statistics.median(times)
+    pair_s = step_s * N / rows  # rows dominate; the fixed LN/bias part is counted once per sample
+    value = fl / pair_s / 1e12
+    line = {
+        "impl": "reference", "metric": metric_name(args.config), "value": value, "unit": "TFLOP/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": pair_s * 1e3,
+        "ms_per_layer": pair_s * 1e3 / (2 if cfg["pair"] else 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args.config, ws),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} of {N} attention rows per layer and step, scaled to the full pair"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(cfg_id):
+    N = CONFIGS[cfg_id]["N"]
+    return f"tri-attn TFLOP/s, start+end pair, N={N}, B=1 (ms/layer reported beside it)"
+
+
+def workload_config(cfg_id, ws):
+    c = CONFIGS[cfg_id]
+    return {"workload": f"config{cfg_id}: {'start+end pair' if c['pair'] else 'start node'} triangle attention, "
+                        f"N={c['N']}, c_z=128, 4x32 heads, {c['dtype']}, B=1",
+            "N": c["N"], "B": 1, "layers_per_step": 2 if c["pair"] else 1,
+            "l2": "pair tensor (N^2 x 512 B) larger than the 126 MB L2 at N>=512; no flush",
+            "parallelism": f"rows{ws}" if ws > 1 else "single"}
+
+
+# ---- B200 arm --------------------------------------------------------------------------------------
+def run_b200(args):
+    from boltz_mlx_b200 import _lib
+    from boltz_mlx_b200.triangle_attention import TriangleAttention, load_params
+
+    ws_n, rank, local = dist_env()
+    if ws_n > 1:
+        from boltz_mlx_b200 import distributed as tdist
+
+        return tdist.bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric_name,
+                                   ClockSampler, physical_gpu_index, peaks)
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    N = cfg["N"]
+    prec = args.precision or cfg["dtype"]
+    dt = _lib.dtype_code(prec)
+    z_h, pm_h, ps, pe = make_config_inputs(args.config)
+    mods = []
+    for starting, p in ((True, ps), (False, pe)):
+        m = TriangleAttention(starting=starting, precision=prec).to(dev)
+        load_params(m, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
+        mods.append(m)
+    packs = [m.packed_weights(dt) for m in mods]
+    z = z_h.to(dev)
+    mask = pm_h.to(dev)
+    t1, t2 = torch.empty_like(z), torch.empty_like(z)
+    wsb = _lib.workspace_bytes(1, N, N, dt)
+    work = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    layers = (1 + int(cfg["pair"]))
+
+    def step(src, mid, dst):
+        _lib.check(L.triattn_forward(src.data_ptr(), mask.data_ptr(), packs[0].data_ptr(), 1, N, 1, 1e9, dt, 1,
+                                     mid.data_ptr(), work.data_ptr(), wsb, sh))
+        if cfg["pair"]:
+            _lib.check(L.triattn_forward(mid.data_ptr(), mask.data_ptr(), packs[1].data_ptr(), 1, N, 0, 1e9, dt, 1,
+                                         dst.data_ptr(), work.data_ptr(), wsb, sh))
+
+    for _ in range(args.warmup):
+        step(z, t1, t2)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "device status word set during warm-up"
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu_index(local)) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step(z, t1, t2)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    step_ms = ev0.elapsed_time(ev1) / args.steps
+    fl = layer_flops(N)
+    pair_flops = fl["total"] * layers
+    value = pair_flops / (step_ms * 1e-3) / 1e12
+
+    # ---- dominant kernel (attention core) timed alone, CUDA events on the launching stream ----
+    _lib.check(L.triattn_mask_prep(mask.data_ptr(), 1, N, 0, 1e9, 0, N, dt, work.data_ptr(), wsb, sh))
+    _lib.check(L.triattn_ln_proj(t1.data_ptr(), packs[1].data_ptr(), 1, N, 0, 0, N, dt, work.data_ptr(), wsb, sh))
+    core_iters = 10
+    for _ in range(2):
+        _lib.check(L.triattn_core(1, N, 0, N, dt, work.data_ptr(), wsb, sh))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(core_iters):
+        _lib.check(L.triattn_core(1, N, 0, N, dt, work.data_ptr(), wsb, sh))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    core_ms = e0.elapsed_time(e1) / core_iters
+    pk, pk_kind = peaks()
+    tensor_peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    achieved = fl["core"] / (core_ms * 1e-3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "core_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(str(N))
+        except ValueError:
+            traffic = None
+
+    # ---- e2e through the C ABI: host pinned buffers, copies inside the timed region ----
+    zh = z_h.pin_memory()
+    mh = pm_h.pin_memory()
+    oh = torch.empty_like(zh).pin_memory()
+    zd, md = torch.empty_like(z), torch.empty_like(mask)
+
+    def e2e_step():
+        zd.copy_(zh, non_blocking=True)
+        md.copy_(mh, non_blocking=True)
+        _lib.check(L.triattn_forward(zd.data_ptr(), md.data_ptr(), packs[0].data_ptr(), 1, N, 1, 1e9, dt, 1,
+                                     t1.data_ptr(), work.data_ptr(), wsb, sh))
+        last = t1
+        if cfg["pair"]:
+            _lib.check(L.triattn_forward(t1.data_ptr(), md.data_ptr(), packs[1].data_ptr(), 1, N, 0, 1e9, dt, 1,
+                                         t2.data_ptr(), work.data_ptr(), wsb, sh))
+            last = t2
+        oh.copy_(last, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_step()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    assert _lib.device_status() == 0, "device status word set"
+
+    # ---- CPU baseline (oracle on the host cores, bounded sample) ----
+    threads = os.cpu_count() or 1
+    cpu_pair_s, sample = cpu_pair_seconds(args.config, threads, budget_s=args.cpu_budget)
+
+    line = {
+        "metric": metric_name(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "ms_per_layer": step_ms / layers,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": prec,
+        "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
+        "config": workload_config(args.config, 1),
+        "roofline": {"bound": "tensor", "kernel": "core_tc (flash attention core)", "achieved": achieved,
+                     "peak": tensor_peak, "unit": "TFLOP/s", "frac": achieved / tensor_peak,
+                     "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic, "core_ms": core_ms,
+                     "algorithmic": f"F_core = 4 N^3 H C = {fl['core']:.4g} FLOP per launch"},
+        "cpu_baseline": {"value": pair_flops / cpu_pair_s / 1e12, "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample, "ms_per_layer": cpu_pair_s * 1e3 / layers},
+        "e2e": {"value": pair_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": zh.numel() * 4 + mh.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4},
+        "gpu_launches": args.steps * layers * 4,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=None)
+    ap.add_argument("--precision", default=None)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.config is None:
+        args.config = 2  # one workload for every GPU count, so the driver's scaling ratios compare like with like
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

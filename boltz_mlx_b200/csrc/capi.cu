@@ -1,0 +1,223 @@
+// extern "C" entry points of libtriattn.so (declared in include/triattn.h): host-side argument
+// validation, workspace layout, stage dispatch on the caller's stream, device status word.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "triattn.h"
+#include "triattn_internal.cuh"
+
+namespace triattn {
+
+__device__ int g_device_status = 0;
+
+// Device address of the status word, resolved once per device (the __device__ variable has one
+// instance per device that loads the library).
+int* device_status_ptr() {
+  static int* cache[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[dev]) {
+    int* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_device_status) != cudaSuccess) return nullptr;
+    cache[dev] = p;
+  }
+  return cache[dev];
+}
+
+}  // namespace triattn
+
+using namespace triattn;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(TRIATTN_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_dims(int B, int N, int dtype) {
+  if (B < 1 || N < 1) return fail(TRIATTN_EINVAL, "B=%d N=%d must be >= 1", B, N);
+  if (N > 16384) return fail(TRIATTN_EUNSUPPORTED, "N=%d above the supported 16384", N);
+  if ((long long)B * HEADS > 65535) return fail(TRIATTN_EUNSUPPORTED, "B=%d too large", B);
+  if (dtype != DT_F32 && dtype != DT_F16 && dtype != DT_BF16) return fail(TRIATTN_EUNSUPPORTED, "dtype %d", dtype);
+  return TRIATTN_OK;
+}
+
+int check_rows(int N, int row_begin, int row_end) {
+  if (row_begin < 0 || row_end > N || row_begin >= row_end)
+    return fail(TRIATTN_EINVAL, "row range [%d,%d) outside [0,%d)", row_begin, row_end, N);
+  if (row_end - row_begin > 65535) return fail(TRIATTN_EUNSUPPORTED, "row range longer than 65535");
+  return TRIATTN_OK;
+}
+
+int check_ws(void* ws, size_t ws_bytes, const Workspace& wl) {
+  if (!ws) return fail(TRIATTN_EINVAL, "workspace is NULL");
+  if (!aligned(ws, 256)) return fail(TRIATTN_EINVAL, "workspace must be 256-byte aligned");
+  if (ws_bytes < wl.total) return fail(TRIATTN_ENOSPACE, "workspace %zu bytes < %zu needed", ws_bytes, wl.total);
+  return TRIATTN_OK;
+}
+
+int check_packed(const void* packed, int dtype) {
+  if (!packed) return fail(TRIATTN_EINVAL, "packed weights are NULL");
+  if (!aligned(packed, 256)) return fail(TRIATTN_EINVAL, "packed weights must be 256-byte aligned");
+  (void)dtype;
+  return TRIATTN_OK;
+}
+
+View pair_view(int N, int starting, int channels) {
+  View v;
+  v.s_batch = (long long)N * N * channels;
+  v.s_row = starting ? (long long)N * channels : channels;
+  v.s_col = starting ? channels : (long long)N * channels;
+  v.row0 = 0;
+  return v;
+}
+
+LayerArgs make_args(int B, int N, int starting, int row_begin, int row_end, float inf, const float* z,
+                    const float* mask, float* out, int add_residual, const void* packed, void* ws, int dtype) {
+  LayerArgs a{};
+  a.B = B; a.N = N; a.row_begin = row_begin; a.row_end = row_end; a.inf = inf;
+  a.z = z; a.zv = pair_view(N, starting, C_IN);
+  a.mask = mask; a.mv = pair_view(N, starting, 1);
+  a.out = out; a.ov = pair_view(N, starting, C_IN);
+  a.add_residual = add_residual;
+  a.packed = static_cast<const unsigned char*>(packed);
+  a.ws = static_cast<unsigned char*>(ws);
+  a.wl = Workspace::make(B, N, row_end - row_begin, dtype);
+  a.status = device_status_ptr();
+  return a;
+}
+
+int finish(cudaError_t e, const char* what) { return e == cudaSuccess ? TRIATTN_OK : cuda_fail(e, what); }
+
+}  // namespace
+
+extern "C" {
+
+const char* triattn_version(void) { return "triattn-b200 0.1 (sm_100a)"; }
+
+const char* triattn_last_error_string(void) { return g_err; }
+
+int triattn_device_status(int* status, int clear) {
+  if (!status) return fail(TRIATTN_EINVAL, "status is NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol");
+  *status = v;
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol");
+  }
+  return TRIATTN_OK;
+}
+
+size_t triattn_packed_weights_bytes(int dtype) { return PackedLayout::bytes(dtype); }
+
+int triattn_pack_weights(const float* ln_w, const float* ln_b, const float* w_q, const float* w_k, const float* w_v,
+                         const float* w_g, const float* g_bias, const float* w_b, const float* w_o, int dtype,
+                         void* packed, size_t packed_bytes, void* stream) {
+  if (dtype != DT_F32 && dtype != DT_F16 && dtype != DT_BF16) return fail(TRIATTN_EUNSUPPORTED, "dtype %d", dtype);
+  if (!ln_w || !ln_b || !w_q || !w_k || !w_v || !w_g || !w_b || !w_o)
+    return fail(TRIATTN_EINVAL, "a weight pointer is NULL");
+  if (int r = check_packed(packed, dtype)) return r;
+  if (packed_bytes < PackedLayout::bytes(dtype))
+    return fail(TRIATTN_ENOSPACE, "packed buffer %zu < %zu bytes", packed_bytes, PackedLayout::bytes(dtype));
+  return finish(launch_pack_weights(ln_w, ln_b, w_q, w_k, w_v, w_g, g_bias, w_b, w_o, dtype,
+                                    static_cast<unsigned char*>(packed), static_cast<cudaStream_t>(stream)),
+                "pack_weights");
+}
+
+size_t triattn_workspace_bytes(int B, int N, int rows, int dtype) {
+  if (B < 1 || N < 1 || rows < 1) return 0;
+  return Workspace::make(B, N, rows, dtype).total;
+}
+
+int triattn_mask_prep(const float* mask, int B, int N, int starting, float inf, int row_begin, int row_end,
+                      int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  LayerArgs a = make_args(B, N, starting, row_begin, row_end, inf, nullptr, mask, nullptr, 0, nullptr, workspace, dtype);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  return finish(launch_mask_prep(a, dtype, static_cast<cudaStream_t>(stream)), "mask_prep");
+}
+
+int triattn_ln_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
+                    int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  if (!z || !aligned(z, 16)) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
+  if (int r = check_packed(packed, dtype)) return r;
+  LayerArgs a = make_args(B, N, starting, row_begin, row_end, 0.f, z, nullptr, nullptr, 0, packed, workspace, dtype);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return finish(dtype == DT_F32 ? launch_ln_proj_f32(a, st) : launch_ln_proj_tc(a, dtype, st), "ln_proj");
+}
+
+int triattn_core(int B, int N, int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  LayerArgs a = make_args(B, N, 1, row_begin, row_end, 0.f, nullptr, nullptr, nullptr, 0, nullptr, workspace, dtype);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return finish(dtype == DT_F32 ? launch_core_f32(a, st) : launch_core_tc(a, dtype, st), "core");
+}
+
+int triattn_out_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
+                     int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  if (!out || !aligned(out, 16)) return fail(TRIATTN_EINVAL, "out must be a 16-byte aligned device pointer");
+  if (add_residual && (!z || !aligned(z, 16))) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
+  if (int r = check_packed(packed, dtype)) return r;
+  LayerArgs a = make_args(B, N, starting, row_begin, row_end, 0.f, z, nullptr, out, add_residual, packed, workspace,
+                          dtype);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return finish(dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st), "out_proj");
+}
+
+int triattn_forward(const float* z, const float* mask, const void* packed, int B, int N, int starting, float inf,
+                    int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (!z || !aligned(z, 16)) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
+  if (!out || !aligned(out, 16)) return fail(TRIATTN_EINVAL, "out must be a 16-byte aligned device pointer");
+  if (int r = check_packed(packed, dtype)) return r;
+  LayerArgs a = make_args(B, N, starting, 0, N, inf, z, mask, out, add_residual, packed, workspace, dtype);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_mask_prep(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "mask_prep");
+  e = dtype == DT_F32 ? launch_ln_proj_f32(a, st) : launch_ln_proj_tc(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "ln_proj");
+  e = dtype == DT_F32 ? launch_core_f32(a, st) : launch_core_tc(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "core");
+  e = dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "out_proj");
+  return TRIATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,118 @@
+// Internal layout contract shared by the kernels and the C ABI: packed-weight offsets, workspace
+// regions and the attention-oriented strided views of z / mask / out.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace triattn {
+
+constexpr int C_IN = 128;
+constexpr int HEADS = 4;
+constexpr int C_HEAD = 32;
+constexpr int HC = HEADS * C_HEAD;  // 128
+constexpr int NPROJ = 4 * HC;       // 512 = q|k|v|g
+constexpr float LN_EPS = 1e-5f;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr int TILE = 128;  // query / key / pair tile of the tensor-core path
+
+constexpr int DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2;
+
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+__host__ __device__ constexpr int round_tile(int n) { return (n + TILE - 1) / TILE * TILE; }
+
+// ---- packed weights ---------------------------------------------------------------------------
+// fp32 section (floats): ln_w[128] ln_b[128] g_b[128] w_b[4][128] w_qkvg[512][128] w_o[128][128]
+// 16-bit section: W_qkvg operand image (K-major, 512 rows x 128 k), W_o operand image (128 x 128).
+struct PackedLayout {
+  static constexpr size_t ln_w = 0;
+  static constexpr size_t ln_b = ln_w + C_IN * 4;
+  static constexpr size_t g_b = ln_b + C_IN * 4;
+  static constexpr size_t w_b = g_b + HC * 4;
+  static constexpr size_t w_qkvg = w_b + HEADS * C_IN * 4;
+  static constexpr size_t w_o = w_qkvg + NPROJ * C_IN * 4;
+  static constexpr size_t f32_end = w_o + C_IN * HC * 4;
+  static constexpr size_t img_qkvg = align_up(f32_end, 1024);
+  static constexpr size_t img_o = img_qkvg + NPROJ * C_IN * 2;
+  static constexpr size_t end16 = img_o + C_IN * HC * 2;
+  static constexpr size_t bytes(int dtype) { return dtype == DT_F32 ? align_up(f32_end, 256) : align_up(end16, 256); }
+};
+
+// ---- workspace ---------------------------------------------------------------------------------
+// 16-bit path (rows R = row_end - row_begin, NT = Np / 128 tiles, Np = N rounded up to 128):
+//   q_img, k_img, v_img : [B][R][H][NT] tiles of 8 KB (128 positions x 32 channels operand image)
+//   g                   : [B][R][N][128] 16-bit
+//   core_img            : [B][R][NT] tiles of 32 KB (128 positions x 128 channels operand image)
+//   bias                : [N][B][H][Np] fp32, log2-domain tri bias (ALL N query rows)
+//   mb                  : [B][R][Np] fp32, log2-domain mask bias; padded keys -1e30
+// fp32 path:
+//   q (pre-scaled by C^-1/2), k, v, g, core : [B][R][N][128] fp32
+//   bias : [N][B][H][Np] fp32 (natural units);  mb : [B][R][Np] fp32 = inf * (mask - 1)
+struct Workspace {
+  int B, N, R, dtype, Np, NT;
+  size_t off_q, off_k, off_v, off_g, off_core, off_bias, off_mb, total;
+
+  __host__ __device__ static Workspace make(int B, int N, int R, int dtype) {
+    Workspace w{};
+    w.B = B; w.N = N; w.R = R; w.dtype = dtype;
+    w.Np = round_tile(N);
+    w.NT = w.Np / TILE;
+    const size_t A = 256;
+    size_t o = 0;
+    if (dtype == DT_F32) {
+      const size_t plane = (size_t)B * R * N * C_IN * 4;
+      w.off_q = o; o = align_up(o + plane, A);
+      w.off_k = o; o = align_up(o + plane, A);
+      w.off_v = o; o = align_up(o + plane, A);
+      w.off_g = o; o = align_up(o + plane, A);
+      w.off_core = o; o = align_up(o + plane, A);
+    } else {
+      const size_t head_tiles = (size_t)B * R * HEADS * w.NT * 8192;
+      w.off_q = o; o = align_up(o + head_tiles, A);
+      w.off_k = o; o = align_up(o + head_tiles, A);
+      w.off_v = o; o = align_up(o + head_tiles, A);
+      w.off_g = o; o = align_up(o + (size_t)B * R * N * C_IN * 2, A);
+      w.off_core = o; o = align_up(o + (size_t)B * R * w.NT * 32768, A);
+    }
+    w.off_bias = o; o = align_up(o + (size_t)N * B * HEADS * w.Np * 4, A);
+    w.off_mb = o; o = align_up(o + (size_t)B * R * w.Np * 4, A);
+    w.total = o;
+    return w;
+  }
+};
+
+// Attention-oriented view of a [B][N][N][ch] tensor: element (b, a, c, ch) lives at
+//   base + b * s_batch + (a - row0) * s_row + c * s_col + ch
+// (starting node: s_row = N*ch, s_col = ch; ending node: s_row = ch, s_col = N*ch).
+struct View {
+  long long s_batch, s_row, s_col;
+  int row0;
+};
+
+struct LayerArgs {
+  int B, N, row_begin, row_end;
+  float inf;
+  const float* z; View zv;     // attention-oriented input
+  const float* mask; View mv;  // attention-oriented mask (nullptr = ones)
+  float* out; View ov;         // attention-oriented output
+  int add_residual;
+  const unsigned char* packed;
+  unsigned char* ws;
+  Workspace wl;
+  int* status;                 // device status word
+};
+
+// launchers (return cudaGetLastError())
+cudaError_t launch_pack_weights(const float* ln_w, const float* ln_b, const float* w_q, const float* w_k,
+                                const float* w_v, const float* w_g, const float* g_bias, const float* w_b,
+                                const float* w_o, int dtype, unsigned char* packed, cudaStream_t st);
+cudaError_t launch_mask_prep(const LayerArgs& a, int dtype, cudaStream_t st);
+cudaError_t launch_ln_proj_f32(const LayerArgs& a, cudaStream_t st);
+cudaError_t launch_core_f32(const LayerArgs& a, cudaStream_t st);
+cudaError_t launch_out_proj_f32(const LayerArgs& a, cudaStream_t st);
+cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
+cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st);
+cudaError_t launch_out_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
+int* device_status_ptr();
+
+}  // namespace triattn

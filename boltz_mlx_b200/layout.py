@@ -1,0 +1,110 @@
+"""Host-side mirror of libtriattn's memory layout (boltz_mlx_b200/csrc/triattn_internal.cuh).
+
+* Operand images: a 128-position x kdim-channel 16-bit tile stored as 8-row x 16-byte core matrices
+  (the sm_100a UMMA no-swizzle K-major layout):
+      byte(row, k) = (row % 8) * 16 + (row // 8) * (16 * kdim) + (k % 8) * 2 + (k // 8) * 128
+* Workspace regions for attention rows [row_begin, row_end) of a B x N layer.
+
+Used by the row-sharded multi-GPU driver (to address the tri-bias rows it exchanges) and by the
+stage-level tests (to decode operand images).  `workspace_bytes` must agree with the library's
+triattn_workspace_bytes (checked by the CPU test-suite).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+TILE = 128
+HEADS, C_HEAD, C_IN = 4, 32, 128
+F32, F16, BF16 = 0, 1, 2
+
+
+def align(x: int, a: int = 256) -> int:
+    return (x + a - 1) // a * a
+
+
+def round_tile(n: int) -> int:
+    return (n + TILE - 1) // TILE * TILE
+
+
+def img_offsets(rows: int, kdim: int) -> np.ndarray:
+    """Byte offset of (row, k) inside an operand image, shape [rows, kdim]."""
+    r = np.arange(rows)[:, None]
+    k = np.arange(kdim)[None, :]
+    return (r % 8) * 16 + (r // 8) * (16 * kdim) + (k % 8) * 2 + (k // 8) * 128
+
+
+@dataclass
+class Workspace:
+    B: int
+    N: int
+    R: int
+    dtype: int
+    Np: int = 0
+    NT: int = 0
+    off_q: int = 0
+    off_k: int = 0
+    off_v: int = 0
+    off_g: int = 0
+    off_core: int = 0
+    off_bias: int = 0
+    off_mb: int = 0
+    total: int = 0
+
+    @classmethod
+    def make(cls, B: int, N: int, R: int, dtype: int) -> "Workspace":
+        w = cls(B, N, R, dtype)
+        w.Np = round_tile(N)
+        w.NT = w.Np // TILE
+        o = 0
+        if dtype == F32:
+            plane = B * R * N * C_IN * 4
+            w.off_q = o; o = align(o + plane)
+            w.off_k = o; o = align(o + plane)
+            w.off_v = o; o = align(o + plane)
+            w.off_g = o; o = align(o + plane)
+            w.off_core = o; o = align(o + plane)
+        else:
+            head_tiles = B * R * HEADS * w.NT * 8192
+            w.off_q = o; o = align(o + head_tiles)
+            w.off_k = o; o = align(o + head_tiles)
+            w.off_v = o; o = align(o + head_tiles)
+            w.off_g = o; o = align(o + B * R * N * C_IN * 2)
+            w.off_core = o; o = align(o + B * R * w.NT * 32768)
+        w.off_bias = o; o = align(o + N * B * HEADS * w.Np * 4)
+        w.off_mb = o; o = align(o + B * R * w.Np * 4)
+        w.total = o
+        return w
+
+    # byte range of the tri-bias rows [r0, r1) (layout [N][B][H][Np] fp32): contiguous per row block
+    def bias_rows(self, r0: int, r1: int) -> tuple[int, int]:
+        row = self.B * HEADS * self.Np * 4
+        return self.off_bias + r0 * row, self.off_bias + r1 * row
+
+
+def workspace_bytes(B: int, N: int, rows: int, dtype: int) -> int:
+    return Workspace.make(B, N, rows, dtype).total
+
+
+def decode_head_images(buf, w: Workspace, off: int):
+    """q/k/v images -> tensor [B, R, H, Np, 32] (16-bit values as float32).  `buf` is a uint8 torch tensor."""
+    import torch
+
+    tdt = torch.bfloat16 if w.dtype == BF16 else torch.float16
+    n = w.B * w.R * HEADS * w.NT * 8192
+    raw = buf[off:off + n].view(tdt).view(w.B, w.R, HEADS, w.NT, 4096)
+    idx = torch.from_numpy(img_offsets(TILE, C_HEAD) // 2).to(buf.device)
+    return raw[..., idx].float().reshape(w.B, w.R, HEADS, w.Np, C_HEAD)
+
+
+def decode_core_images(buf, w: Workspace):
+    """core images -> tensor [B, R, Np, 128]."""
+    import torch
+
+    tdt = torch.bfloat16 if w.dtype == BF16 else torch.float16
+    n = w.B * w.R * w.NT * 32768
+    raw = buf[w.off_core:w.off_core + n].view(tdt).view(w.B, w.R, w.NT, 16384)
+    idx = torch.from_numpy(img_offsets(TILE, C_IN) // 2).to(buf.device)
+    return raw[..., idx].float().reshape(w.B, w.R, w.Np, C_IN)

@@ -1,0 +1,129 @@
+/*
+ * triattn.h -- C ABI of the B200 (sm_100a) pairformer triangle-attention library (libtriattn.so).
+ *
+ * One triangle-attention layer (starting node or ending node, forward only) of Boltz-2's
+ * pairformer: z[B,N,N,128] fp32, pair mask [B,N,N], 4 heads x 32 head dim, parameters under the
+ * reference's names (layer_norm.{weight,bias}, linear.weight [4,128], mha.linear_{q,k,v,g,o}.weight).
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer unless stated otherwise; the caller allocates every
+ *     output, the packed weights and the workspace.  The library never allocates or frees memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream).  Calls are
+ *     asynchronous: they validate arguments on the host, enqueue kernels and return.
+ *   - Tensors are dense and row-major ("contiguous"): z/out [B][N][N][128] fp32, mask [B][N][N] fp32.
+ *   - Return value: TRIATTN_OK or an error code below.  No call traps or asserts on the device;
+ *     kernels record device-side failures (a bounded wait that ran out) in a status word that
+ *     triattn_device_status() reads.
+ *   - dtype selects the arithmetic of the layer: TRIATTN_F32 = fp32 everywhere (SIMT, the
+ *     reference's fp32 path, max-rel <= 1e-5); TRIATTN_F16 / TRIATTN_BF16 = 16-bit operands on the
+ *     tcgen05 tensor cores with fp32 accumulation, fp32 softmax statistics and an fp32 residual.
+ *
+ * Reference interfaces replaced (paths inside jackryan225/boltz-mlx):
+ *   triattn_forward      <- TriangleAttention.__call__        boltz_mlx/layers/triangular_attention/attention.py:27-93
+ *                           (+ the residual add of PairformerLayer, boltz_mlx/layers/pairformer.py:86-87)
+ *   triattn_mask_prep    <- nax_tri_inputs mask bias            boltz_mlx/kernels_nax.py:477-503 / attention.py:85
+ *   triattn_ln_proj      <- layer_norm + fused projection       boltz_mlx/kernels.py:482-507, attention.py:47-53,69,
+ *                           (pair_proj16 + tri-bias GEMM)       boltz_mlx/kernels_nax3.py:1625-1634, attention.py:145-149
+ *   triattn_core         <- tri_attention_fused / tri_attention_nax  boltz_mlx/kernels.py:902-945,
+ *                                                                     boltz_mlx/kernels_nax.py:506-558
+ *   triattn_out_proj     <- linear_o / lin16 / linear_addln      attention.py:89, boltz_mlx/kernels.py:1287-1370,
+ *                                                                 boltz_mlx/kernels_nax3.py:320-354
+ *   triattn_pack_weights <- w16 fused fp16 weight cache          boltz_mlx/kernels.py:1349-1357
+ */
+#ifndef TRIATTN_H
+#define TRIATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TRIATTN_API __attribute__((visibility("default")))
+#else
+#define TRIATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------- */
+#define TRIATTN_OK 0
+#define TRIATTN_EINVAL 1       /* null pointer, bad size, bad alignment, bad row range          */
+#define TRIATTN_EUNSUPPORTED 2 /* dtype / configuration not supported by this build             */
+#define TRIATTN_ECUDA 3        /* a CUDA runtime call or launch failed (triattn_last_error_string) */
+#define TRIATTN_EDEVICE 4      /* a kernel recorded a device-side failure (bounded wait ran out) */
+#define TRIATTN_ENOSPACE 5     /* workspace or packed-weight buffer too small                    */
+
+/* ---- dtypes ------------------------------------------------------------------------------- */
+#define TRIATTN_F32 0
+#define TRIATTN_F16 1
+#define TRIATTN_BF16 2
+
+/* Fixed layer geometry of Boltz-2's triangle attention (attention.py:15, pairformer.py:51-52). */
+#define TRIATTN_C_IN 128
+#define TRIATTN_HEADS 4
+#define TRIATTN_C_HEAD 32
+
+/* Library version string (static storage). */
+TRIATTN_API const char* triattn_version(void);
+
+/* Human-readable text of the last host-side error on the calling thread (static storage). */
+TRIATTN_API const char* triattn_last_error_string(void);
+
+/* Read the device status word of the current device (0 = ok); clear it when `clear` != 0.
+ * Synchronises the device.  Returns TRIATTN_OK and writes the word to *status. */
+TRIATTN_API int triattn_device_status(int* status, int clear);
+
+/* ---- weights ------------------------------------------------------------------------------ */
+/* Bytes of the packed-weight buffer for `dtype`. */
+TRIATTN_API size_t triattn_packed_weights_bytes(int dtype);
+
+/* Pack one module's parameters (all DEVICE fp32, reference [out, in] Linear layout):
+ *   ln_w, ln_b [128]; w_q, w_k, w_v, w_g [128,128]; g_bias [128] or NULL (the reference has none);
+ *   w_b [4,128] (the module's `linear`, tri-bias projection); w_o [128,128].
+ * Writes fp32 copies plus, for 16-bit dtypes, the tensor-core operand images of W_qkvg [512,128]
+ * and W_o [128,128].  Done once per module; the result is reused by every call. */
+TRIATTN_API int triattn_pack_weights(const float* ln_w, const float* ln_b, const float* w_q, const float* w_k,
+                         const float* w_v, const float* w_g, const float* g_bias, const float* w_b,
+                         const float* w_o, int dtype, void* packed, size_t packed_bytes, void* stream);
+
+/* ---- workspace ---------------------------------------------------------------------------- */
+/* Bytes of workspace for attention rows [row_begin, row_end) of a B x N layer (rows = row_end -
+ * row_begin; the tri-bias region always covers all N rows).  Needs 256-byte alignment. */
+TRIATTN_API size_t triattn_workspace_bytes(int B, int N, int rows, int dtype);
+
+/* ---- one layer ---------------------------------------------------------------------------- */
+/* out = y (add_residual = 0) or z + y (add_residual = 1), y = TriangleAttention(z, mask).
+ * starting = 1: starting node; 0: ending node (attention over the transposed pair layout, read
+ * and written in place -- z^T is never materialised).  mask may be NULL (all ones).  out may
+ * alias z when add_residual = 1 (in-place residual stream).  inf: the reference's 1e9. */
+TRIATTN_API int triattn_forward(const float* z, const float* mask, const void* packed, int B, int N, int starting,
+                    float inf, int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* ---- stages (row-range granularity: the reference's row chunking, attention.py:55-68) ------
+ * All stages address attention rows a in [row_begin, row_end) of the full-size z / mask / out. */
+
+/* Mask bias of the attention rows: inf * (mask - 1) per (row, key), keys padded to a tile. */
+TRIATTN_API int triattn_mask_prep(const float* mask, int B, int N, int starting, float inf, int row_begin, int row_end,
+                      int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* LayerNorm + q|k|v|g projection of rows [row_begin,row_end) and their tri-bias rows. */
+TRIATTN_API int triattn_ln_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
+                    int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Flash attention core with tri bias, mask bias, online softmax and sigmoid gate; needs the
+ * tri-bias rows of ALL N rows in the workspace. */
+TRIATTN_API int triattn_core(int B, int N, int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Output projection (+ residual) of rows [row_begin,row_end), written in z's orientation. */
+TRIATTN_API int triattn_out_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
+                     int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRIATTN_H */

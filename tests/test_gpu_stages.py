@@ -1,0 +1,133 @@
+"""GPU: each stage of the 16-bit tensor-core path, through the C ABI, against a torch fp32 computation
+of the same stage on the same inputs (16-bit rounding points reproduced).  A layout or descriptor
+mistake shows up here in the stage that makes it."""
+
+import pytest
+import torch
+
+from boltz_mlx_b200 import _lib, layout
+from oracle.triattn_ref import C_HEAD, HC, HEADS, LN_EPS, make_params
+from tests._util import module, rand_mask
+
+pytestmark = pytest.mark.gpu
+LOG2E = 1.4426950408889634
+
+
+def t16(precision):
+    return torch.bfloat16 if precision == "bf16" else torch.float16
+
+
+def run_ln_proj(N, precision, starting=True, B=1, seed=0, mask=None):
+    dt = _lib.dtype_code(precision)
+    g = torch.Generator().manual_seed(seed + N)
+    z = torch.randn(B, N, N, 128, generator=g)
+    p = make_params(seed + N, gate_bias=1.0, ln_identity=False)
+    mod = module(p, starting, precision)
+    packed = mod.packed_weights(dt)
+    w = layout.Workspace.make(B, N, N, dt)
+    ws = torch.full((w.total,), 0xFF, dtype=torch.uint8, device="cuda")  # poison: unwritten bytes are NaN
+    zc = z.cuda()
+    mc = None if mask is None else mask.cuda()
+    L = _lib.lib()
+    st = _lib.stream_handle(zc.device)
+    _lib.check(L.triattn_mask_prep(_lib.ptr(mc), B, N, int(starting), 1e9, 0, N, dt, ws.data_ptr(), ws.numel(), st))
+    _lib.check(L.triattn_ln_proj(zc.data_ptr(), packed.data_ptr(), B, N, int(starting), 0, N, dt, ws.data_ptr(),
+                                 ws.numel(), st))
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    return dict(z=z, p=p, mod=mod, packed=packed, w=w, ws=ws, zc=zc, dt=dt, mask=mask, B=B, N=N, starting=starting)
+
+
+def ref_projection(ctx, precision):
+    z, p = ctx["z"], ctx["p"]
+    x = z if ctx["starting"] else z.transpose(1, 2)
+    mu = x.mean(-1, keepdim=True)
+    var = ((x - mu) ** 2).mean(-1, keepdim=True)
+    xn = (x - mu) / torch.sqrt(var + LN_EPS) * p["ln_w"] + p["ln_b"]
+    r = lambda t: t.to(t16(precision)).float()
+    W = torch.cat([p["w_q"], p["w_k"], p["w_v"], p["w_g"]], 0)
+    h = r(xn) @ r(W).T  # 16-bit operands, fp32 accumulate
+    tb = xn @ p["w_b"].T  # fp32 SIMT dot in the kernel
+    return xn, h, tb
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+@pytest.mark.parametrize("N,starting", [(9, True), (128, True), (200, False), (129, True)])
+def test_ln_proj_stage(precision, N, starting):
+    ctx = run_ln_proj(N, precision, starting)
+    w, ws, B = ctx["w"], ctx["ws"], ctx["B"]
+    xn, h, tb = ref_projection(ctx, precision)
+    rt = 1e-2 if precision == "bf16" else 2e-3
+    for i, off in enumerate((w.off_q, w.off_k, w.off_v)):
+        img = layout.decode_head_images(ws, w, off).cpu()  # [B, R, H, Np, 32]
+        ref = h[..., i * HC:(i + 1) * HC].reshape(B, N, N, HEADS, C_HEAD).permute(0, 1, 3, 2, 4)
+        got = img[:, :, :, :N]
+        torch.testing.assert_close(got, ref.to(t16(precision)).float(), rtol=rt, atol=rt * 0.1,
+                                   msg=lambda m: f"image {i}: {m}")
+        assert torch.all(img[:, :, :, N:] == 0), "padded positions must be zero"
+    gbuf = ws[w.off_g:w.off_g + B * N * N * 128 * 2].view(t16(precision)).view(B, N, N, 128).float().cpu()
+    torch.testing.assert_close(gbuf, (h[..., 3 * HC:] + 1.0).to(t16(precision)).float(), rtol=rt, atol=rt * 0.1)
+    bias = ws[w.off_bias:w.off_bias + N * B * HEADS * w.Np * 4].view(torch.float32).view(N, B, HEADS, w.Np).cpu()
+    ref_b = (tb * LOG2E).permute(1, 0, 3, 2)  # [q=a][b][h][k=c]
+    torch.testing.assert_close(bias[..., :N], ref_b, rtol=1e-4, atol=1e-5)
+    assert torch.all(bias[..., N:] == 0)
+
+
+def ref_core(ctx, precision):
+    """Softmax attention on the decoded 16-bit q/k/v/g images, fp32, log2 domain (kernels_nax.py:376-406)."""
+    w, ws, B, N = ctx["w"], ctx["ws"], ctx["B"], ctx["N"]
+    q = layout.decode_head_images(ws, w, w.off_q)[:, :, :, :N].cpu()
+    k = layout.decode_head_images(ws, w, w.off_k)[:, :, :, :N].cpu()
+    v = layout.decode_head_images(ws, w, w.off_v)[:, :, :, :N].cpu()
+    g = ws[w.off_g:w.off_g + B * N * N * 128 * 2].view(t16(precision)).view(B, N, N, 128).float().cpu()
+    bias = ws[w.off_bias:w.off_bias + N * B * HEADS * w.Np * 4].view(torch.float32).view(N, B, HEADS, w.Np).cpu()
+    mb = ws[w.off_mb:w.off_mb + B * N * w.Np * 4].view(torch.float32).view(B, N, w.Np).cpu()
+    s = torch.einsum("bahqd,bahkd->bahqk", q, k) * (C_HEAD ** -0.5 * LOG2E)
+    s = s + mb[:, :, None, None, :N] + bias[..., :N].permute(1, 2, 0, 3)[:, None]
+    s = s - s.amax(-1, keepdim=True)
+    pr = torch.exp2(s)
+    o = torch.einsum("bahqk,bahkd->bahqd", pr, v) / pr.sum(-1, keepdim=True)
+    o = o.permute(0, 1, 3, 2, 4).reshape(B, N, N, HC)
+    return o * torch.sigmoid(g)
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+@pytest.mark.parametrize("N,masked", [(9, False), (128, True), (200, True), (300, False)])
+def test_core_stage(precision, N, masked):
+    g = torch.Generator().manual_seed(77 + N)
+    mask = rand_mask(g, 1, N, "rows_cols") if masked else None
+    ctx = run_ln_proj(N, precision, True, mask=mask)
+    w, ws = ctx["w"], ctx["ws"]
+    _lib.check(_lib.lib().triattn_core(1, N, 0, N, ctx["dt"], ws.data_ptr(), ws.numel(),
+                                       _lib.stream_handle(ws.device)))
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    got = layout.decode_core_images(ws, w)[:, :, :N].cpu()
+    ref = ref_core(ctx, precision)
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs()
+    scale = ref.abs().max()
+    assert err.max() <= 2e-2 * scale and err.mean() <= 2e-3 * scale, (float(err.max()), float(err.mean()), float(scale))
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+@pytest.mark.parametrize("starting,residual", [(True, False), (False, True)])
+def test_out_proj_stage(precision, starting, residual):
+    N = 140
+    ctx = run_ln_proj(N, precision, starting)
+    w, ws, L = ctx["w"], ctx["ws"], _lib.lib()
+    st = _lib.stream_handle(ws.device)
+    _lib.check(L.triattn_core(1, N, 0, N, ctx["dt"], ws.data_ptr(), ws.numel(), st))
+    out = torch.full_like(ctx["zc"], float("nan"))
+    _lib.check(L.triattn_out_proj(ctx["zc"].data_ptr(), ctx["packed"].data_ptr(), 1, N, int(starting), 0, N, ctx["dt"],
+                                  int(residual), out.data_ptr(), ws.data_ptr(), ws.numel(), st))
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    core = layout.decode_core_images(ws, w)[:, :, :N].cpu()
+    wo = ctx["p"]["w_o"].to(t16(precision)).float()
+    y = core @ wo.T  # attention orientation
+    if not starting:
+        y = y.transpose(1, 2)
+    if residual:
+        y = y + ctx["z"]
+    torch.testing.assert_close(out.cpu(), y, rtol=1e-4, atol=1e-4)

@@ -1,0 +1,85 @@
+"""CPU emulation of the tensor-core operand addressing (in the spirit of the reference's
+tests/nax3_emul.py): the byte layout the producers write must be exactly what the UMMA shared-memory
+descriptors of the consumers read, for every MMA the kernels issue."""
+
+import numpy as np
+import pytest
+
+from boltz_mlx_b200.layout import TILE, Workspace, img_offsets
+
+
+def kmajor_desc_addr(start, lbo, sbo, rows, kdim):
+    """Bytes read by a no-swizzle K-major descriptor for a rows x kdim (16-bit) operand."""
+    r = np.arange(rows)[:, None]
+    k = np.arange(kdim)[None, :]
+    return start + (r % 8) * 16 + (r // 8) * sbo + (k % 8) * 2 + (k // 8) * lbo
+
+
+def mnmajor_desc_addr(start, lbo, sbo, mn, kdim):
+    """Bytes read by a no-swizzle MN-major descriptor: element (mn, k)."""
+    m = np.arange(mn)[:, None]
+    k = np.arange(kdim)[None, :]
+    return start + (k % 8) * 16 + (k // 8) * lbo + (m % 8) * 2 + (m // 8) * sbo
+
+
+@pytest.mark.parametrize("kdim", [32, 128])
+def test_image_is_a_dense_bijection(kdim):
+    off = img_offsets(TILE, kdim)
+    assert off.min() == 0 and off.max() == TILE * kdim * 2 - 2
+    assert len(np.unique(off)) == TILE * kdim
+    assert np.all(off % 2 == 0)
+    # every 8-row x 8-element core matrix is one contiguous 128-byte block
+    for r0 in range(0, TILE, 8):
+        for k0 in range(0, kdim, 8):
+            blk = np.sort(off[r0:r0 + 8, k0:k0 + 8].ravel())
+            assert blk[0] % 128 == 0 and np.array_equal(np.diff(blk), np.full(63, 2))
+
+
+def test_qk_mma_k_steps():
+    """S = Q K^T: two K=16 instructions at start + 256 B (lbo 128, sbo 512) cover the 32-channel image."""
+    off = img_offsets(TILE, 32)
+    for ks in range(2):
+        got = kmajor_desc_addr(ks * 256, 128, 512, TILE, 16)
+        assert np.array_equal(got, off[:, ks * 16:(ks + 1) * 16])
+
+
+def test_pv_mma_reads_v_image_as_mn_major():
+    """O = P V: B = V (N = 32 channels, K = 128 keys) MN-major with lbo 512 / sbo 128; instruction j
+    (keys 16j..16j+15) starts at +1024 j.  The V image is written K-major by ln_proj (row = key)."""
+    off = img_offsets(TILE, 32)  # off[key, ch]
+    for j in range(TILE // 16):
+        got = mnmajor_desc_addr(j * 1024, 512, 128, 32, 16)  # [ch, key-in-step]
+        assert np.array_equal(got, off[j * 16:(j + 1) * 16, :].T)
+
+
+@pytest.mark.parametrize("n_half", [0, 1])
+def test_projection_mma_w_halves(n_half):
+    """D[128 x 512] in two N=256 MMAs: B half h starts at +65536 B, K steps of 16 at +256 B."""
+    woff = img_offsets(512, 128)
+    aoff = img_offsets(TILE, 128)
+    for ks in range(8):
+        a = kmajor_desc_addr(ks * 256, 128, 2048, TILE, 16)
+        assert np.array_equal(a, aoff[:, ks * 16:(ks + 1) * 16])
+        b = kmajor_desc_addr(n_half * 65536 + ks * 256, 128, 2048, 256, 16)
+        assert np.array_equal(b, woff[n_half * 256:(n_half + 1) * 256, ks * 16:(ks + 1) * 16])
+
+
+def test_p_tmem_columns_pack_key_pairs():
+    """P (128 queries x 128 keys, 16-bit) lives in TMEM columns [0,64): column c of lane q holds keys
+    2c (low half) and 2c+1 (high half); TS instruction j reads columns 8j..8j+7 = keys 16j..16j+15."""
+    cols = np.arange(64)
+    keys_lo, keys_hi = 2 * cols, 2 * cols + 1
+    for j in range(8):
+        sel = slice(8 * j, 8 * j + 8)
+        assert set(keys_lo[sel]) | set(keys_hi[sel]) == set(range(16 * j, 16 * j + 16))
+
+
+@pytest.mark.parametrize("N", [1, 127, 128, 129, 1024, 2048])
+def test_workspace_regions_disjoint_and_aligned(N):
+    for dtype in (0, 1, 2):
+        w = Workspace.make(2, N, N, dtype)
+        offs = [w.off_q, w.off_k, w.off_v, w.off_g, w.off_core, w.off_bias, w.off_mb, w.total]
+        assert offs == sorted(offs)
+        assert all(o % 256 == 0 for o in offs)
+        b0, b1 = w.bias_rows(0, N)
+        assert b0 == w.off_bias and b1 <= w.off_mb
