@@ -20,7 +20,8 @@ DTYPES = {"fp32": F32, "float32": F32, "fp16": F16, "float16": F16, "f16": F16, 
 EXPORTED = [
     "triattn_version", "triattn_last_error_string", "triattn_device_status", "triattn_packed_weights_bytes",
     "triattn_pack_weights", "triattn_workspace_bytes", "triattn_forward", "triattn_mask_prep",
-    "triattn_ln_proj", "triattn_core", "triattn_out_proj",
+    "triattn_ln_proj", "triattn_core", "triattn_out_proj", "triattn_mask_prep_v", "triattn_ln_proj_v",
+    "triattn_out_proj_v",
 ]
 
 
@@ -65,6 +66,11 @@ def lib() -> ctypes.CDLL:
         L.triattn_ln_proj.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_core.argtypes = [_i, _i, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_out_proj.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]
+        _l = ctypes.c_int64
+        L.triattn_mask_prep_v.argtypes = [_vp, _l, _l, _l, _i, _i, _f, _i, _i, _i, _vp, _sz, _vp]
+        L.triattn_ln_proj_v.argtypes = [_vp, _l, _l, _l, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+        L.triattn_out_proj_v.argtypes = [_vp, _l, _l, _l, _vp, _l, _l, _l, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz,
+                                         _vp]
         for name in EXPORTED:
             if name not in ("triattn_version", "triattn_last_error_string", "triattn_packed_weights_bytes",
                             "triattn_workspace_bytes"):

@@ -199,6 +199,64 @@ int triattn_out_proj(const float* z, const void* packed, int B, int N, int start
   return finish(dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st), "out_proj");
 }
 
+static int check_view(const char* name, const void* p, int64_t sb, int64_t sr, int64_t sc, bool vec4) {
+  if (!p) return fail(TRIATTN_EINVAL, "%s is NULL", name);
+  if (sb < 0 || sr < 0 || sc < 0) return fail(TRIATTN_EINVAL, "%s: negative stride", name);
+  if (vec4 && (!aligned(p, 16) || sb % 4 || sr % 4 || sc % 4))
+    return fail(TRIATTN_EINVAL, "%s: base must be 16-byte aligned and strides multiples of 4 elements", name);
+  return TRIATTN_OK;
+}
+
+static View make_view(int64_t sb, int64_t sr, int64_t sc, int row0) {
+  View v;
+  v.s_batch = sb; v.s_row = sr; v.s_col = sc; v.row0 = row0;
+  return v;
+}
+
+int triattn_mask_prep_v(const float* mask, int64_t s_batch, int64_t s_row, int64_t s_col, int B, int N, float inf,
+                        int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  if (mask && s_batch < 0) return fail(TRIATTN_EINVAL, "mask: negative stride");
+  LayerArgs a = make_args(B, N, 1, row_begin, row_end, inf, nullptr, mask, nullptr, 0, nullptr, workspace, dtype);
+  a.mv = make_view(s_batch, s_row, s_col, row_begin);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  return finish(launch_mask_prep(a, dtype, static_cast<cudaStream_t>(stream)), "mask_prep_v");
+}
+
+int triattn_ln_proj_v(const float* z, int64_t s_batch, int64_t s_row, int64_t s_col, const void* packed, int B, int N,
+                      int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  if (int r = check_view("z", z, s_batch, s_row, s_col, true)) return r;
+  if (int r = check_packed(packed, dtype)) return r;
+  LayerArgs a = make_args(B, N, 1, row_begin, row_end, 0.f, z, nullptr, nullptr, 0, packed, workspace, dtype);
+  a.zv = make_view(s_batch, s_row, s_col, row_begin);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return finish(dtype == DT_F32 ? launch_ln_proj_f32(a, st) : launch_ln_proj_tc(a, dtype, st), "ln_proj_v");
+}
+
+int triattn_out_proj_v(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, float* out,
+                       int64_t os_batch, int64_t os_row, int64_t os_col, const void* packed, int B, int N,
+                       int row_begin, int row_end, int dtype, int add_residual, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (int r = check_rows(N, row_begin, row_end)) return r;
+  if (int r = check_view("out", out, os_batch, os_row, os_col, true)) return r;
+  if (add_residual)
+    if (int r = check_view("z", z, zs_batch, zs_row, zs_col, true)) return r;
+  if (int r = check_packed(packed, dtype)) return r;
+  LayerArgs a = make_args(B, N, 1, row_begin, row_end, 0.f, z, nullptr, out, add_residual, packed, workspace, dtype);
+  a.zv = make_view(zs_batch, zs_row, zs_col, row_begin);
+  a.ov = make_view(os_batch, os_row, os_col, row_begin);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return finish(dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st), "out_proj_v");
+}
+
 int triattn_forward(const float* z, const float* mask, const void* packed, int B, int N, int starting, float inf,
                     int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes, void* stream) {
   if (int r = check_dims(B, N, dtype)) return r;

@@ -39,15 +39,18 @@ struct PackedLayout {
 };
 
 // ---- workspace ---------------------------------------------------------------------------------
-// 16-bit path (rows R = row_end - row_begin, NT = Np / 128 tiles, Np = N rounded up to 128):
+// The tri-bias region comes first, at offset 0, so it sits at the same place whatever row count a
+// call is made with: row chunks of different sizes (and the ranks of a row-sharded layer) fill and
+// read one shared [N][B][H][Np] bias.  Per-row regions follow, laid out for R = row_end - row_begin.
+//   bias                : [N][B][H][Np] fp32 tri bias of ALL N query rows (log2 domain on the 16-bit
+//                         path, natural units on the fp32 path)
+// 16-bit path (NT = Np / 128 tiles, Np = N rounded up to 128):
 //   q_img, k_img, v_img : [B][R][H][NT] tiles of 8 KB (128 positions x 32 channels operand image)
 //   g                   : [B][R][N][128] 16-bit
 //   core_img            : [B][R][NT] tiles of 32 KB (128 positions x 128 channels operand image)
-//   bias                : [N][B][H][Np] fp32, log2-domain tri bias (ALL N query rows)
 //   mb                  : [B][R][Np] fp32, log2-domain mask bias; padded keys -1e30
 // fp32 path:
-//   q (pre-scaled by C^-1/2), k, v, g, core : [B][R][N][128] fp32
-//   bias : [N][B][H][Np] fp32 (natural units);  mb : [B][R][Np] fp32 = inf * (mask - 1)
+//   q (pre-scaled by C^-1/2), k, v, g, core : [B][R][N][128] fp32;  mb : [B][R][Np] = inf * (mask - 1)
 struct Workspace {
   int B, N, R, dtype, Np, NT;
   size_t off_q, off_k, off_v, off_g, off_core, off_bias, off_mb, total;
@@ -59,6 +62,7 @@ struct Workspace {
     w.NT = w.Np / TILE;
     const size_t A = 256;
     size_t o = 0;
+    w.off_bias = o; o = align_up(o + (size_t)N * B * HEADS * w.Np * 4, A);
     if (dtype == DT_F32) {
       const size_t plane = (size_t)B * R * N * C_IN * 4;
       w.off_q = o; o = align_up(o + plane, A);
@@ -74,7 +78,6 @@ struct Workspace {
       w.off_g = o; o = align_up(o + (size_t)B * R * N * C_IN * 2, A);
       w.off_core = o; o = align_up(o + (size_t)B * R * w.NT * 32768, A);
     }
-    w.off_bias = o; o = align_up(o + (size_t)N * B * HEADS * w.Np * 4, A);
     w.off_mb = o; o = align_up(o + (size_t)B * R * w.Np * 4, A);
     w.total = o;
     return w;

@@ -3,7 +3,8 @@
 * Operand images: a 128-position x kdim-channel 16-bit tile stored as 8-row x 16-byte core matrices
   (the sm_100a UMMA no-swizzle K-major layout):
       byte(row, k) = (row % 8) * 16 + (row // 8) * (16 * kdim) + (k % 8) * 2 + (k // 8) * 128
-* Workspace regions for attention rows [row_begin, row_end) of a B x N layer.
+* Workspace regions for attention rows [row_begin, row_end) of a B x N layer; the tri-bias region is
+  first, at offset 0, whatever the row count.
 
 Used by the row-sharded multi-GPU driver (to address the tri-bias rows it exchanges) and by the
 stage-level tests (to decode operand images).  `workspace_bytes` must agree with the library's
@@ -59,6 +60,8 @@ class Workspace:
         w.Np = round_tile(N)
         w.NT = w.Np // TILE
         o = 0
+        # tri bias first: one fixed place for every row count (row chunks / ranks share it)
+        w.off_bias = o; o = align(o + N * B * HEADS * w.Np * 4)
         if dtype == F32:
             plane = B * R * N * C_IN * 4
             w.off_q = o; o = align(o + plane)
@@ -73,7 +76,6 @@ class Workspace:
             w.off_v = o; o = align(o + head_tiles)
             w.off_g = o; o = align(o + B * R * N * C_IN * 2)
             w.off_core = o; o = align(o + B * R * w.NT * 32768)
-        w.off_bias = o; o = align(o + N * B * HEADS * w.Np * 4)
         w.off_mb = o; o = align(o + B * R * w.Np * 4)
         w.total = o
         return w

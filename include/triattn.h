@@ -117,6 +117,25 @@ TRIATTN_API int triattn_ln_proj(const float* z, const void* packed, int B, int N
 TRIATTN_API int triattn_core(int B, int N, int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* ---- strided-view stages (row-sharded / column-blocked pair tensors) ------------------------
+ * The _v variants address an attention-oriented VIEW of a pair tensor instead of a dense [B][N][N]
+ * one: element (b, a, c, ch) of the view lives at
+ *     base + b*s_batch + (a - row_begin)*s_row + c*s_col + ch          (in elements)
+ * for attention rows a in [row_begin, row_end) and columns c in [0, N).  For the pair tensors
+ * s_row and s_col must be multiples of 4 (16-byte rows).  A rank that owns rows [r0, r1) of z
+ * passes its local shard with s_row = N*128, s_col = 128; after an all-to-all it owns columns and
+ * passes the received block with s_row = 128, s_col = rows_per_rank*128. */
+TRIATTN_API int triattn_mask_prep_v(const float* mask, int64_t s_batch, int64_t s_row, int64_t s_col, int B, int N,
+                                    float inf, int row_begin, int row_end, int dtype, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+TRIATTN_API int triattn_ln_proj_v(const float* z, int64_t s_batch, int64_t s_row, int64_t s_col, const void* packed,
+                                  int B, int N, int row_begin, int row_end, int dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+TRIATTN_API int triattn_out_proj_v(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, float* out,
+                                   int64_t os_batch, int64_t os_row, int64_t os_col, const void* packed, int B, int N,
+                                   int row_begin, int row_end, int dtype, int add_residual, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* Output projection (+ residual) of rows [row_begin,row_end), written in z's orientation. */
 TRIATTN_API int triattn_out_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
                      int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,

@@ -78,8 +78,12 @@ def test_p_tmem_columns_pack_key_pairs():
 def test_workspace_regions_disjoint_and_aligned(N):
     for dtype in (0, 1, 2):
         w = Workspace.make(2, N, N, dtype)
-        offs = [w.off_q, w.off_k, w.off_v, w.off_g, w.off_core, w.off_bias, w.off_mb, w.total]
+        offs = [w.off_bias, w.off_q, w.off_k, w.off_v, w.off_g, w.off_core, w.off_mb, w.total]
         assert offs == sorted(offs)
         assert all(o % 256 == 0 for o in offs)
         b0, b1 = w.bias_rows(0, N)
-        assert b0 == w.off_bias and b1 <= w.off_mb
+        assert b0 == w.off_bias == 0 and b1 <= w.off_q
+        # the bias region does not move with the row count of a call
+        for R in (1, max(1, N // 3), N):
+            assert Workspace.make(2, N, R, dtype).off_bias == 0
+            assert Workspace.make(2, N, R, dtype).off_q == w.off_q
