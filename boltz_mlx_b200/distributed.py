@@ -1,0 +1,222 @@
+"""Row-sharded triangle attention over the GPUs of one node (one process per GPU, NCCL over NVLink).
+
+The reference runs on one device and bounds memory by row chunking: the tri bias is computed from
+ALL rows, then attention runs over chunks of rows (attention.py:55-68, kernels.py:1158-1168).  The
+multi-GPU form distributes those row chunks:
+
+* z (and the residual stream) is sharded by rows i: rank p owns rows [p*R, (p+1)*R), R = N / P.
+* Starting node: LN + projection of the local rows, their tri-bias rows, ONE all-gather of the tri
+  bias ([N][B][H][Np] fp32, rows contiguous), local attention core and output projection + residual.
+* Ending node: attention row a is column a of z, so the pair tensor is re-sharded by columns with
+  an all-to-all (rows_to_cols), the same stages run on the column block through strided views
+  (no transposed copy of z is materialised by the kernels), the tri bias is all-gathered, and the
+  updated column block goes back to row sharding with a second all-to-all (cols_to_rows).
+
+The exchange steps are plain torch.distributed collectives, so the host logic also runs on CPU
+ranks with the gloo backend (tests/test_distributed_cpu.py).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .layout import C_IN, HEADS, Workspace
+
+
+def shard_rows(N: int, P: int, rank: int) -> tuple[int, int]:
+    if N % P:
+        raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED, f"N={N} must be divisible by the {P} ranks")
+    R = N // P
+    return rank * R, (rank + 1) * R
+
+
+def gather_bias(ws: torch.Tensor, w: Workspace, r0: int, r1: int, group=None) -> None:
+    """All-gather the tri-bias rows [r0, r1) of every rank into the full bias region (in place)."""
+    b0, b1 = w.bias_rows(0, w.N)
+    full = ws[b0:b1]
+    l0, l1 = w.bias_rows(r0, r1)
+    local = ws[l0:l1]
+    dist.all_gather_into_tensor(full, local.clone() if not full.is_cuda else local, group=group)
+
+
+def rows_to_cols(z_loc: torch.Tensor, P: int, send: torch.Tensor, recv: torch.Tensor, group=None) -> torch.Tensor:
+    """Row shard z_loc [R, N, C] -> column block zt [N, R, C] (zt[i, a] = z[i, r0 + a]) by all-to-all.
+
+    send / recv are [P, R, R, C] buffers; the result is `recv` viewed as [N, R, C]."""
+    R, N, Cc = z_loc.shape
+    send.copy_(z_loc.view(R, P, R, Cc).transpose(0, 1))
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.view(N, R, Cc)
+
+
+def cols_to_rows(zt: torch.Tensor, P: int, recv: torch.Tensor, z_loc_out: torch.Tensor, group=None) -> None:
+    """Column block zt [N, R, C] -> row shard z_loc_out [R, N, C] by all-to-all (inverse of rows_to_cols)."""
+    N, R, Cc = zt.shape
+    dist.all_to_all_single(recv, zt.reshape(P, R, R, Cc).contiguous(), group=group)
+    z_loc_out.view(R, P, R, Cc).copy_(recv.transpose(0, 1))
+
+
+class ShardedPair:
+    """One start+end triangle-attention pair on a row-sharded pair tensor (B = 1)."""
+
+    def __init__(self, N: int, precision: str, device: torch.device, group=None, inf: float = 1e9):
+        self.N, self.inf, self.device, self.group = N, inf, device, group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.r0, self.r1 = shard_rows(N, self.P, self.rank)
+        self.R = self.r1 - self.r0
+        self.dt = _lib.dtype_code(precision)
+        self.w = Workspace.make(1, N, self.R, self.dt)
+        self.ws = torch.empty(self.w.total, dtype=torch.uint8, device=device)
+        self.send = torch.empty(self.P, self.R, self.R, C_IN, device=device)
+        self.recv = torch.empty_like(self.send)
+        self.recv2 = torch.empty_like(self.send)
+        self.L = _lib.lib()
+
+    def _st(self):
+        return _lib.stream_handle(self.device)
+
+    def start(self, z_loc: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
+        """z_loc [R, N, 128] (rows r0..r1 of z) += TriAttStart(z) for those rows, in place."""
+        L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
+        ws, nb = self.ws.data_ptr(), self.ws.numel()
+        mptr = None if mask is None else mask.data_ptr() + r0 * N * 4
+        _lib.check(L.triattn_mask_prep_v(mptr, N * N, N, 1, 1, N, self.inf, r0, r1, dt, ws, nb, st))
+        _lib.check(L.triattn_ln_proj_v(z_loc.data_ptr(), R * N * C_IN, N * C_IN, C_IN, packed.data_ptr(), 1, N, r0, r1,
+                                       dt, ws, nb, st))
+        gather_bias(self.ws, self.w, r0, r1, self.group)
+        _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
+        zp = z_loc.data_ptr()
+        _lib.check(L.triattn_out_proj_v(zp, R * N * C_IN, N * C_IN, C_IN, zp, R * N * C_IN, N * C_IN, C_IN,
+                                        packed.data_ptr(), 1, N, r0, r1, dt, 1, ws, nb, st))
+
+    def end(self, z_loc: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
+        """z_loc [R, N, 128] += TriAttEnd(z) for rows r0..r1, via the column block of z."""
+        L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
+        ws, nb = self.ws.data_ptr(), self.ws.numel()
+        zt = rows_to_cols(z_loc, self.P, self.send, self.recv, self.group)  # [N, R, 128]
+        # attention row a (global, in [r0, r1)) is column a of z: x_att[a][c] = zt[c][a - r0]
+        mptr = None if mask is None else mask.data_ptr() + r0 * 4
+        _lib.check(L.triattn_mask_prep_v(mptr, N * N, 1, N, 1, N, self.inf, r0, r1, dt, ws, nb, st))
+        zp = zt.data_ptr()
+        _lib.check(L.triattn_ln_proj_v(zp, N * R * C_IN, C_IN, R * C_IN, packed.data_ptr(), 1, N, r0, r1, dt, ws, nb,
+                                       st))
+        gather_bias(self.ws, self.w, r0, r1, self.group)
+        _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
+        _lib.check(L.triattn_out_proj_v(zp, N * R * C_IN, C_IN, R * C_IN, zp, N * R * C_IN, C_IN, R * C_IN,
+                                        packed.data_ptr(), 1, N, r0, r1, dt, 1, ws, nb, st))
+        cols_to_rows(zt, self.P, self.recv2, z_loc, self.group)
+
+    def pair(self, z_loc, mask, packed_start, packed_end) -> None:
+        self.start(z_loc, mask, packed_start)
+        self.end(z_loc, mask, packed_end)
+
+    def nvlink_bytes_per_pair(self) -> int:
+        """Bytes each rank sends over NVLink per pair: 2 bias all-gathers + 2 all-to-alls of fp32 z blocks."""
+        bias = (self.P - 1) * self.R * HEADS * self.w.Np * 4
+        a2a = (self.P - 1) * self.R * self.R * C_IN * 4
+        return 2 * bias + 2 * a2a
+
+
+def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric_name, ClockSampler,
+                  physical_gpu_index, peaks):
+    """bench.py --gpus P under torchrun: one start+end pair on the row-sharded pair tensor per step."""
+    from datetime import timedelta
+
+    from .triangle_attention import TriangleAttention, load_params
+
+    ws_n = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        z_h, pm_h, ps, pe = make_config_inputs(args.config)
+        N = z_h.shape[1]
+        prec = args.precision or {0: "fp32", 1: "fp16"}.get(args.config, "bf16")
+        sp = ShardedPair(N, prec, dev)
+        packs = []
+        for starting, p in ((True, ps), (False, pe)):
+            m = TriangleAttention(starting=starting, precision=prec).to(dev)
+            load_params(m, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
+            packs.append(m.packed_weights(sp.dt))
+        z0 = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
+        mask = pm_h[0].contiguous().to(dev)
+        z_loc = torch.empty_like(z0)
+
+        def step():
+            z_loc.copy_(z0)
+            sp.pair(z_loc, mask, packs[0], packs[1])
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream = torch.cuda.current_stream(dev)
+        with ClockSampler(physical_gpu_index(local)) as clk:
+            dist.barrier()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(args.steps):
+                step()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            dist.barrier()
+        ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        step_ms = float(ms)
+        fl = layer_flops(N)
+        pair_flops = 2 * fl["total"]
+        value = pair_flops / (step_ms * 1e-3) / 1e12
+
+        # e2e: host shard + mask copied in, shard copied out, every step
+        zh = z_h[0, sp.r0:sp.r1].contiguous().pin_memory()
+        mh = pm_h[0].contiguous().pin_memory()
+        oh = torch.empty_like(zh).pin_memory()
+
+        def e2e_step():
+            z_loc.copy_(zh, non_blocking=True)
+            mask.copy_(mh, non_blocking=True)
+            sp.pair(z_loc, mask, packs[0], packs[1])
+            oh.copy_(z_loc, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        n_e2e = max(1, min(args.steps, 5))
+        ev0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        e2e = torch.tensor([ev0.elapsed_time(ev1) / n_e2e], device=dev)
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+        status = torch.tensor([_lib.device_status()], device=dev)
+        dist.all_reduce(status, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            line = {
+                "metric": metric_name(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": ws_n,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "ms_per_layer": step_ms / 2,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": prec,
+                "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
+                "config": workload_config(args.config, ws_n),
+                "nvlink_bytes_per_rank_per_step": sp.nvlink_bytes_per_pair(),
+                "e2e": {"value": pair_flops / (float(e2e) * 1e-3) / 1e12, "unit": "TFLOP/s",
+                        "ms_per_step": float(e2e), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
+                        "d2h_bytes_per_step": oh.numel() * 4 * ws_n},
+                "gpu_launches": args.steps * 2 * 4,
+                "device_status": int(status),
+                "clocks": clk.summary(),
+            }
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()

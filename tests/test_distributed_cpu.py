@@ -1,0 +1,86 @@
+"""CPU, multi-process (gloo): the row-sharded layer's exchange steps -- the tri-bias all-gather and
+the all-to-all row <-> column re-sharding -- against single-process references, world sizes 2 and 4.
+The same functions drive the NCCL path on the GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from boltz_mlx_b200.distributed import cols_to_rows, gather_bias, rows_to_cols, shard_rows
+from boltz_mlx_b200.layout import Workspace
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, P, port, N, errq):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=P)
+        C = 8
+        g = torch.Generator().manual_seed(0)
+        z = torch.randn(N, N, C, generator=g)  # every rank builds the same full tensor
+        r0, r1 = shard_rows(N, P, rank)
+        R = r1 - r0
+        send = torch.empty(P, R, R, C)
+        recv = torch.empty_like(send)
+        recv2 = torch.empty_like(send)
+        z_loc = z[r0:r1].clone()
+        zt = rows_to_cols(z_loc, P, send, recv)
+        assert torch.equal(zt, z[:, r0:r1]), "rows_to_cols"
+        zt.mul_(2.0).add_(float(rank))  # a column-block update
+        out = torch.empty_like(z_loc)
+        cols_to_rows(zt, P, recv2, out)
+        ref = z * 2.0
+        for q in range(P):
+            ref[:, q * R:(q + 1) * R] += float(q)
+        assert torch.equal(out, ref[r0:r1]), "cols_to_rows"
+        # tri-bias all-gather over the workspace layout
+        for dtype in (0, 2):
+            w = Workspace.make(1, N, R, dtype)
+            ws = torch.zeros(w.total, dtype=torch.uint8)
+            l0, l1 = w.bias_rows(r0, r1)
+            ws[l0:l1] = (rank + 1) * torch.ones(l1 - l0, dtype=torch.uint8)
+            ws[l1:] = 77  # per-row regions must not be touched
+            gather_bias(ws, w, r0, r1)
+            for q in range(P):
+                a, b = w.bias_rows(q * R, (q + 1) * R)
+                assert torch.all(ws[a:b] == q + 1), "gather_bias"
+            b0, b1 = w.bias_rows(0, N)
+            assert torch.all(ws[b1:] == 77)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+@pytest.mark.parametrize("P,N", [(2, 8), (4, 12), (2, 256)])
+def test_exchange_steps(P, N):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, P, port, N, errq)) for r in range(P)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def test_shard_rows_requires_divisibility():
+    assert shard_rows(1024, 8, 3) == (384, 512)
+    with pytest.raises(NotImplementedError):
+        shard_rows(1000, 3, 0)
