@@ -36,6 +36,16 @@ namespace {
 
 thread_local char g_err[512] = "";
 
+}  // namespace
+
+// Record a host-side error (read back by triattn_last_error_string) and return its code.
+int triattn::record_error(int code, const char* what, const char* detail) {
+  snprintf(g_err, sizeof(g_err), "%s: %s", what, detail);
+  return code;
+}
+
+namespace {
+
 int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);

@@ -117,5 +117,6 @@ cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 cudaError_t launch_out_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 int* device_status_ptr();
+int record_error(int code, const char* what, const char* detail);
 
 }  // namespace triattn

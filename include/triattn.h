@@ -141,6 +141,18 @@ TRIATTN_API int triattn_out_proj(const float* z, const void* packed, int B, int 
                      int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* ---- allocation-free layer ----------------------------------------------------------------
+ * No counterpart in the reference.  triattn_forward without a workspace argument, for callers that
+ * cannot allocate device memory at run time (a plugin host that forbids cudaMalloc after start-up,
+ * a process whose device memory is owned by another allocator, a fixed device footprint).  The
+ * scratch is a 48 MiB array inside the library that every GPU loading it holds until exit; calls
+ * whose triattn_workspace_bytes(B, N, N, dtype) exceeds it (about N > 128 at B = 1) return
+ * TRIATTN_ENOSPACE.  The first call on a device looks the array up (make it before any stream
+ * capture); calls share the array, so calls that overlap on the GPU race.  Allocates nothing. */
+TRIATTN_API int triattn_forward_noalloc(const float* z, const float* mask, const void* packed, int B, int N,
+                                        int starting, float inf, int dtype, int add_residual, float* out,
+                                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif
