@@ -90,6 +90,7 @@ __global__ void mask_prep_kernel(const float* __restrict__ mask, View mv, int B,
 }
 
 cudaError_t launch_mask_prep(const LayerArgs& a, int dtype, cudaStream_t st) {
+  if (dtype != DT_F32) return launch_mask_prep_tc(a, st);
   const int R = a.row_end - a.row_begin;
   float* mb = reinterpret_cast<float*>(a.ws + a.wl.off_mb);
   dim3 grid((a.wl.Np + 255) / 256, R, a.B);
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(64) core_f32_kernel(LayerArgs args) {
   __shared__ float Ms[64];
   const int tid = threadIdx.x;
   const int j = blockIdx.x * 64 + tid;
-  const int al = blockIdx.y, a = args.row_begin + al;
+  const int al = blockIdx.y;
   const int b = blockIdx.z / HEADS, h = blockIdx.z % HEADS;
   const int N = args.N, R = args.row_end - args.row_begin, Np = args.wl.Np;
   const bool valid = j < N;

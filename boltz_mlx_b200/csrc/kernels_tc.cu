@@ -4,8 +4,9 @@
 // Data flow of one layer (attention orientation x[a][c]; ending node: x[a][c] = z[c][a], read in
 // place through strides):
 //   ln_proj_tc : z rows -> LN (fp32 stats) -> xn 16-bit operand image in smem -> UMMA with the
-//                W_qkvg image (512 x 128) -> q, k, v operand images (8 KB per 128-position tile and
-//                head), g (row-major 16-bit); tri bias (fp32 SIMT dot from fp32 xn, x log2e).
+//                W_qkvg image (512 x 128) -> q (x C^-1/2 log2 e), k, v (fp16) operand images (8 KB per
+//                128-position tile and head), g (row-major 16-bit); tri bias (fp32 SIMT dot from fp32
+//                xn, x log2 e, stored fp16 in 128 x 128 blocks).
 //   core_tc    : per (b, row a, head h, 128-query tile): S = Q K^T (UMMA, SS) in TMEM ->
 //                log2-domain logits fma(S, C^-1/2 log2e, mask bias) + tri bias, online softmax
 //                (fp32) -> P (16-bit) stored to TMEM -> O_part = P V (UMMA, A from TMEM) ->
@@ -59,7 +60,7 @@ __global__ void __launch_bounds__(256, 1) ln_proj_tc_kernel(LayerArgs args) {
   const int ct = blockIdx.x, c0 = ct * TILE;
   const int al = blockIdx.y, a = args.row_begin + al;
   const int b = blockIdx.z;
-  const int N = args.N, R = args.row_end - args.row_begin, Np = args.wl.Np, NT = args.wl.NT;
+  const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT;
   const float* P = reinterpret_cast<const float*>(args.packed);
   int* status = args.status;
 
@@ -121,13 +122,20 @@ __global__ void __launch_bounds__(256, 1) ln_proj_tc_kernel(LayerArgs args) {
   fence_proxy_async_smem();
   __syncthreads();
 
-  // ---- tri bias rows: bias[a][b][h][c] (log2 domain; padded columns 0) ----
-  {
-    float* bias = reinterpret_cast<float*>(args.ws + args.wl.off_bias);
-    for (int idx = tid; idx < HEADS * TILE; idx += 256) {
-      const int hh = idx / TILE, r = idx % TILE, c = c0 + r;
-      bias[(((size_t)a * args.B + b) * HEADS + hh) * Np + c] = c < N ? sBias[idx] * LOG2E : 0.0f;
+  // ---- tri-bias rows of attention row a: fp16, log2 domain, 128 x 128 block layout [k/8][q][8];
+  //      one 16-byte chunk = 8 consecutive keys of one head (padded keys 0) ----
+  if (tid < HEADS * (TILE / 8)) {
+    const int hh = tid / (TILE / 8), kg = tid % (TILE / 8);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r0 = kg * 8 + 2 * i;
+      const float v0 = c0 + r0 < N ? sBias[hh * TILE + r0] * LOG2E : 0.0f;
+      const float v1 = c0 + r0 + 1 < N ? sBias[hh * TILE + r0 + 1] * LOG2E : 0.0f;
+      w[i] = H16<__half>::pack(v0, v1);
     }
+    *reinterpret_cast<uint4*>(args.ws + args.wl.off_bias + bias16_off(a, c0 + kg * 8, b, hh, args.B, NT)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
 
   // ---- MMA: D[128 x 512] = xn[128 x 128] * W_qkvg[512 x 128]^T, two N=256 halves ----
@@ -163,20 +171,37 @@ __global__ void __launch_bounds__(256, 1) ln_proj_tc_kernel(LayerArgs args) {
       uint32_t acc[32];
       tmem_ld32(tmem_addr(tbase, quad * 32, tt * 128 + hh * 32), acc);
       tmem_ld_wait();
-      if (tt < 3) {
-        const size_t off = (tt == 0 ? args.wl.off_q : tt == 1 ? args.wl.off_k : args.wl.off_v) +
-                           ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
-        unsigned char* img = args.ws + off;
+      if (tt == 0 || tt == 1) {
+        // q (pre-scaled by C^-1/2 log2 e: the core's S is then in log2 units) and k: K-major images
+        const float sc = tt == 0 ? QSCALE_L2 : 1.0f;
+        unsigned char* img = args.ws + (tt == 0 ? args.wl.off_q : args.wl.off_k) +
+                             ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
 #pragma unroll
         for (int d = 0; d < C_HEAD; d += 8) {
           uint4 pk = make_uint4(0u, 0u, 0u, 0u);
           if (valid) {
-            pk.x = H16<T>::pack(__uint_as_float(acc[d + 0]), __uint_as_float(acc[d + 1]));
-            pk.y = H16<T>::pack(__uint_as_float(acc[d + 2]), __uint_as_float(acc[d + 3]));
-            pk.z = H16<T>::pack(__uint_as_float(acc[d + 4]), __uint_as_float(acc[d + 5]));
-            pk.w = H16<T>::pack(__uint_as_float(acc[d + 6]), __uint_as_float(acc[d + 7]));
+            pk.x = H16<T>::pack(__uint_as_float(acc[d + 0]) * sc, __uint_as_float(acc[d + 1]) * sc);
+            pk.y = H16<T>::pack(__uint_as_float(acc[d + 2]) * sc, __uint_as_float(acc[d + 3]) * sc);
+            pk.z = H16<T>::pack(__uint_as_float(acc[d + 4]) * sc, __uint_as_float(acc[d + 5]) * sc);
+            pk.w = H16<T>::pack(__uint_as_float(acc[d + 6]) * sc, __uint_as_float(acc[d + 7]) * sc);
           }
           *reinterpret_cast<uint4*>(img + img_off(r, d, C_HEAD)) = pk;
+        }
+      } else if (tt == 2) {
+        // v: fp16 in every 16-bit mode (the P.V product runs in fp16), saturated to the fp16 range,
+        // MN-major image read by the P.V MMA
+        unsigned char* img = args.ws + args.wl.off_v + ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
+        auto sat = [](uint32_t u) { return fminf(fmaxf(__uint_as_float(u), -65504.f), 65504.f); };
+#pragma unroll
+        for (int d = 0; d < C_HEAD; d += 8) {
+          uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+          if (valid) {
+            pk.x = H16<__half>::pack(sat(acc[d + 0]), sat(acc[d + 1]));
+            pk.y = H16<__half>::pack(sat(acc[d + 2]), sat(acc[d + 3]));
+            pk.z = H16<__half>::pack(sat(acc[d + 4]), sat(acc[d + 5]));
+            pk.w = H16<__half>::pack(sat(acc[d + 6]), sat(acc[d + 7]));
+          }
+          *reinterpret_cast<uint4*>(img + vimg_off(r, d)) = pk;
         }
       } else if (valid) {
         const float* gb = P + PackedLayout::g_b / 4 + hh * C_HEAD;
@@ -212,204 +237,397 @@ cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 }
 
 // =================================================================================================
-// Flash core.  CTA = 128 queries of one (b, attention row a, head h); 128 threads, thread t owns
-// query qt*128 + t = TMEM lane t.  TMEM: S / P at columns [0,128), O partial at [128,160).
+// Mask bias + key-tile classes (16-bit path).  One CTA per (attention row, batch), 128 threads.
+//   mb[b][row][k] = log2(e) * inf * (mask - 1)  (k < N),  -1e30 for padded keys
+//   ts[b][row][kt] = 0 every key of the tile valid, 1 every key masked and the row has a valid key
+//   elsewhere (the tile contributes exactly 0 and is skipped), 2 otherwise (mask bias applied; a
+//   row with no valid key at all keeps every tile, which makes it attend uniformly, as in fp32).
 // =================================================================================================
-constexpr int CORE_SMEM_FIXED = 8192 * 5 + 128;  // Q, K[2], V[2], barriers + TMEM slot
+__global__ void __launch_bounds__(128) mask_prep_tc_kernel(LayerArgs args) {
+  __shared__ uint8_t cls[TILE];  // NT <= 128 (N <= 16384)
+  __shared__ int any_valid;
+  const int tid = threadIdx.x;
+  const int al = blockIdx.x, a = args.row_begin + al, b = blockIdx.y;
+  const int N = args.N, R = args.row_end - args.row_begin, Np = args.wl.Np, NT = args.wl.NT;
+  float* mb = reinterpret_cast<float*>(args.ws + args.wl.off_mb) + ((size_t)b * R + al) * Np;
+  if (tid == 0) any_valid = 0;
+  __syncthreads();
+  const View mv = args.mv;
+  for (int kt = 0; kt < NT; ++kt) {
+    const int k = kt * TILE + tid;
+    float v = -1e30f;
+    if (k < N) {
+      const float m =
+          args.mask ? args.mask[b * mv.s_batch + (long long)(a - mv.row0) * mv.s_row + (long long)k * mv.s_col] : 1.0f;
+      v = args.inf * (m - 1.0f) * LOG2E;
+    }
+    mb[k] = v;
+    const int n_valid = __syncthreads_count(k < N && v == 0.0f);
+    const int n_bad = __syncthreads_count(!(k < N && v == 0.0f));
+    if (tid == 0) {
+      cls[kt] = n_valid == 0 ? 1 : (n_bad == 0 ? 0 : 2);
+      if (n_valid) any_valid = 1;
+    }
+  }
+  __syncthreads();
+  uint8_t* ts = args.ws + args.wl.off_ts + ((size_t)b * R + al) * NT;
+  for (int kt = tid; kt < NT; kt += blockDim.x) ts[kt] = any_valid ? cls[kt] : 2;
+}
+
+cudaError_t launch_mask_prep_tc(const LayerArgs& a, cudaStream_t st) {
+  dim3 grid(a.row_end - a.row_begin, a.B);
+  mask_prep_tc_kernel<<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// =================================================================================================
+// Flash core.  CTA = (batch b, head h, 128-query tile qt, group of RG attention rows); the tri-bias
+// tile of (h, qt, kt) is loaded once per key tile and shared by the RG rows.
+//   16 warps = four softmax warpgroups; warpgroup j owns row j of the group (TMEM lanes = queries).
+//   Each row's leader thread issues that row's work itself: the bulk copies of its Q, K and V tiles
+//   (one slot each, refilled as soon as the MMA that read the slot has completed) and its MMAs
+//   (S = Q K^T, then O = P V).  The tri-bias stages (double-buffered) are refilled by whichever warp
+//   is the last of the 16 to finish reading a stage (an arrival counter in shared memory).
+// TMEM (512 columns): row j owns columns [128 j, 128 j + 128): S (fp32, log2 units) -> x (after the
+// biases) -> P (fp16 pairs in columns 0..63) and the P.V partial (columns 64..111: 32 channels + the
+// row sum from V's ones column).  O is accumulated in registers with a lazy rescale.
+// =================================================================================================
+constexpr int CG_RG = 4;
+constexpr int CG_SOFTMAX_WARPS = 4 * CG_RG;
+constexpr int CG_THREADS = CG_SOFTMAX_WARPS * 32;
+constexpr int CG_SQ = 0;                           // RG Q tiles, 8 KB each
+constexpr int CG_SB = CG_SQ + CG_RG * 8192;        // 2 tri-bias stages, 32 KB each (fp16)
+constexpr int CG_SMB = CG_SB + 2 * 32768;          // 2 stages x RG mask-bias slices of 512 B
+constexpr int CG_SK = CG_SMB + 2 * CG_RG * 512;    // one K slot per row, 8 KB
+constexpr int CG_SV = CG_SK + CG_RG * 8192;        // one V slot per row, 12 KB (8 KB V + 4 KB ones/zeros)
+constexpr int CG_BAR = CG_SV + CG_RG * 12288;
+constexpr int CG_CLS = CG_BAR + 512;               // RG x 128 key-tile classes
+constexpr int CG_CNT = CG_CLS + CG_RG * TILE;      // 2 tri-bias stage arrival counters
+constexpr int CG_SMEM = CG_CNT + 16;
+static_assert(CG_SMEM <= 232448, "core shared memory");
+
+// barrier slots
+constexpr int B_BF = 0, B_QF = 2, B_KF = B_QF + CG_RG, B_VF = B_KF + CG_RG, B_SF = B_VF + CG_RG,
+              B_OF = B_SF + CG_RG, B_COUNT = B_OF + CG_RG;
+static_assert(B_COUNT * 8 + 16 <= 512, "barrier area");
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// x0 + lo(w), x1 + hi(w): fp16 tri bias added to fp32 logits in one mixed-precision add each.
+__device__ __forceinline__ void add_f16_pair(float& x0, float& x1, uint32_t w) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
+      : "+f"(x0), "+f"(x1)
+      : "r"(w));
+}
+
+// 2^(x0 - m), 2^(x1 - m) as an fp16 pair (low half x0): one packed fp32 subtract, one conversion to
+// an fp16 pair, one packed 16-bit exponential.
+__device__ __forceinline__ uint32_t exp2_pair_f16(float x0, float x1, uint64_t neg_m2) {
+  uint32_t r;
+  asm("{\n\t.reg .b64 d;\n\t.reg .f32 a, b;\n\t.reg .b32 t;\n\t"
+      "mov.b64 d, {%1, %2};\n\tadd.rn.f32x2 d, d, %3;\n\tmov.b64 {a, b}, d;\n\t"
+      "cvt.rn.f16x2.f32 t, b, a;\n\tex2.approx.f16x2 %0, t;\n\t}"
+      : "=r"(r)
+      : "f"(x0), "f"(x1), "l"(neg_m2));
+  return r;
+}
+
+// Named barrier of one softmax warpgroup (ids 1..RG; 0 is __syncthreads).
+__device__ __forceinline__ void wg_sync(int j) { asm volatile("bar.sync %0, 128;" ::"r"(j + 1) : "memory"); }
 
 template <typename T>
-__global__ void __launch_bounds__(128) core_tc_kernel(LayerArgs args) {
+__global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* sQ = smem;
-  unsigned char* sK[2] = {smem + 8192, smem + 16384};
-  unsigned char* sV[2] = {smem + 24576, smem + 32768};
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 40960);  // q, kv0, kv1, mma
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 40960 + 64);
-  float* sMB = reinterpret_cast<float*>(smem + CORE_SMEM_FIXED);  // mask-bias row [Np]
-  uint64_t* bar_q = bars;
-  uint64_t* bar_kv = bars + 1;
-  uint64_t* bar_mma = bars + 3;
-
-  const int tid = threadIdx.x, warp = tid >> 5;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + CG_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + CG_BAR + B_COUNT * 8);
+  uint8_t* scls = smem + CG_CLS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qt = blockIdx.x;
-  const int al = blockIdx.y;
+  const int g0 = blockIdx.y * CG_RG;  // first local row of the group
   const int b = blockIdx.z / HEADS, h = blockIdx.z % HEADS;
-  const int N = args.N, R = args.row_end - args.row_begin, Np = args.wl.Np, NT = args.wl.NT;
-  const int q = qt * TILE + tid;
-  const bool valid = q < N;
-  const int qc = valid ? q : N - 1;
+  const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT, Np = args.wl.Np;
   int* status = args.status;
 
-  const size_t head_tile0 = (((size_t)b * R + al) * HEADS + h) * NT;
-  const unsigned char* qimg = args.ws + args.wl.off_q + (head_tile0 + qt) * 8192;
-  const unsigned char* kimg = args.ws + args.wl.off_k + head_tile0 * 8192;
-  const unsigned char* vimg = args.ws + args.wl.off_v + head_tile0 * 8192;
-  const float* mbrow = reinterpret_cast<const float*>(args.ws + args.wl.off_mb) + ((size_t)b * R + al) * Np;
-  const float* tb = reinterpret_cast<const float*>(args.ws + args.wl.off_bias) +
-                    (((size_t)qc * args.B + b) * HEADS + h) * Np;
-
+  // ---- set-up: barriers, V-slot tails, key-tile classes, TMEM ----
+  int* bias_cnt = reinterpret_cast<int*>(smem + CG_CNT);
   if (tid == 0) {
-    mbar_init(bar_q, 1);
-    mbar_init(bar_kv + 0, 1);
-    mbar_init(bar_kv + 1, 1);
-    mbar_init(bar_mma, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(bar + B_BF + i, 1);
+    for (int j = 0; j < CG_RG; ++j) {
+      mbar_init(bar + B_QF + j, 1);
+      mbar_init(bar + B_KF + j, 1);
+      mbar_init(bar + B_VF + j, 1);
+      mbar_init(bar + B_SF + j, 1);
+      mbar_init(bar + B_OF + j, 1);
+    }
+    bias_cnt[0] = bias_cnt[1] = 0;
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(tslot, 256);
+  // V slot tail: channel group 4 = (1, 0, ..., 0) per key (the ones column that yields the row
+  // sum), channel group 5 = zeros.  2 x 2 KB per slot, never overwritten by the V copies.
+  for (int i = tid; i < CG_RG * 1024; i += CG_THREADS) {
+    const int stg = i / 1024, w = i % 1024;
+    uint32_t* tail = reinterpret_cast<uint32_t*>(smem + CG_SV + stg * 12288 + 8192);
+    tail[w] = (w < 512 && (w & 3) == 0) ? 0x00003C00u : 0u;  // fp16 1.0 in the low half of each key's first word
+  }
+  // key-tile classes (0 all valid, 1 skip, 2 mixed; 3 = row outside the range)
+  for (int i = tid; i < CG_RG * TILE; i += CG_THREADS) {
+    const int j = i / TILE, kt = i % TILE;
+    scls[i] = (g0 + j < R && kt < NT) ? args.ws[args.wl.off_ts + ((size_t)b * R + g0 + j) * NT + kt] : 3;
+  }
+  fence_proxy_async_smem();
+  if (warp == 0) tmem_alloc(tslot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  const uint32_t tS = tbase, tO = tbase + 128;
-
+  const size_t head0 = ((size_t)b * R) * HEADS + h;  // + row * HEADS -> (b, row, h)
+  int nrow = 0;
+#pragma unroll
+  for (int jj = 0; jj < CG_RG; ++jj) nrow += (g0 + jj < R);
+  const unsigned char* bias_blk = args.ws + args.wl.off_bias + (((size_t)qt * args.B + b) * HEADS + h) * NT * 32768;
+  const float* mb_all = reinterpret_cast<const float*>(args.ws + args.wl.off_mb);
+  // tri-bias tile kt (+ the mask-bias slices of the group's rows) -> stage kt & 1
+  auto load_bias = [&](int kt) {
+    const int bs = kt & 1;
+    mbar_arrive_expect_tx(bar + B_BF + bs, 32768 + nrow * 512);
+    bulk_g2s(smem + CG_SB + bs * 32768, bias_blk + (size_t)kt * 32768, 32768, bar + B_BF + bs);
+    for (int jj = 0; jj < CG_RG; ++jj)
+      if (g0 + jj < R)
+        bulk_g2s(smem + CG_SMB + (bs * CG_RG + jj) * 512, mb_all + ((size_t)b * R + g0 + jj) * Np + kt * TILE, 512,
+                 bar + B_BF + bs);
+  };
   if (tid == 0) {
-    mbar_arrive_expect_tx(bar_q, 8192 + Np * 4);
-    bulk_g2s(sQ, qimg, 8192, bar_q);
-    bulk_g2s(sMB, mbrow, Np * 4, bar_q);
-    for (int s = 0; s < 2 && s < NT; ++s) {
-      mbar_arrive_expect_tx(bar_kv + s, 16384);
-      bulk_g2s(sK[s], kimg + (size_t)s * 8192, 8192, bar_kv + s);
-      bulk_g2s(sV[s], vimg + (size_t)s * 8192, 8192, bar_kv + s);
-    }
+    load_bias(0);
+    if (NT > 1) load_bias(1);
   }
 
-  constexpr uint32_t idS = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
-  constexpr uint32_t idO = make_idesc_f16(128, C_HEAD, H16<T>::is_bf16, 0, 1);
-  const float c_l2 = 0.17677669529663687f * LOG2E;  // C^-1/2 * log2(e)
-  float m = -INFINITY, l = 0.f;
-  float o[C_HEAD];
-#pragma unroll
-  for (int d = 0; d < C_HEAD; ++d) o[d] = 0.f;
-  uint32_t mph = 0;
-  mbar_wait(bar_q, 0, status, DEV_TIMEOUT_TMA);
-  __syncwarp();
-
-  for (int kt = 0; kt < NT; ++kt) {
-    const int s = kt & 1;
-    if (tid == 0) {
-      mbar_wait(bar_kv + s, (kt >> 1) & 1, status, DEV_TIMEOUT_TMA);
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < C_HEAD / 16; ++ks) {
-        const uint64_t ad = smem_desc_noswizzle(smem_u32(sQ) + ks * 256, 128, 16 * C_HEAD);
-        const uint64_t bd = smem_desc_noswizzle(smem_u32(sK[s]) + ks * 256, 128, 16 * C_HEAD);
-        umma_ss(tS, ad, bd, idS, ks > 0 ? 1u : 0u);
-      }
-      umma_commit(bar_mma);
-    }
-    __syncwarp();
-    mbar_wait(bar_mma, mph, status, DEV_TIMEOUT_MMA);
-    __syncwarp();
-    mph ^= 1;
-    tc_fence_after();
-
-    // ---- logits (log2 domain) and row max ----
-    float x[TILE];
-#pragma unroll
-    for (int cch = 0; cch < 4; ++cch) {
-      uint32_t sr[32];
-      tmem_ld32(tmem_addr(tS, warp * 32, cch * 32), sr);
-      tmem_ld_wait();
-#pragma unroll
-      for (int kk = 0; kk < 32; kk += 4) {
-        const int k = cch * 32 + kk;
-        const float4 t4 = __ldg(reinterpret_cast<const float4*>(tb + kt * TILE + k));
-        const float4 m4 = *reinterpret_cast<const float4*>(sMB + kt * TILE + k);
-        x[k + 0] = fmaf(__uint_as_float(sr[kk + 0]), c_l2, m4.x) + t4.x;
-        x[k + 1] = fmaf(__uint_as_float(sr[kk + 1]), c_l2, m4.y) + t4.y;
-        x[k + 2] = fmaf(__uint_as_float(sr[kk + 2]), c_l2, m4.z) + t4.z;
-        x[k + 3] = fmaf(__uint_as_float(sr[kk + 3]), c_l2, m4.w) + t4.w;
-      }
-    }
-    float rmax = x[0];
-#pragma unroll
-    for (int k = 1; k < TILE; ++k) rmax = fmaxf(rmax, x[k]);
-    const float m_new = fmaxf(m, rmax);
-    const float alpha = ex2(m - m_new);
-    m = m_new;
-    float sum = 0.f;
-#pragma unroll
-    for (int cch = 0; cch < 4; ++cch) {
-      uint32_t pk[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float p0 = ex2(x[cch * 32 + 2 * i] - m_new);
-        const float p1 = ex2(x[cch * 32 + 2 * i + 1] - m_new);
-        sum += p0 + p1;
-        pk[i] = H16<T>::pack(p0, p1);
-      }
-      tmem_st16(tmem_addr(tS, warp * 32, cch * 16), pk);
-    }
-    tmem_st_wait();
-    l = l * alpha + sum;
-#pragma unroll
-    for (int d = 0; d < C_HEAD; ++d) o[d] *= alpha;
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- O_part = P V ----
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int j = 0; j < TILE / 16; ++j) {
-        const uint64_t bd = smem_desc_noswizzle(smem_u32(sV[s]) + j * 1024, 512, 128);
-        umma_ts(tO, tS + j * 8, bd, idO, j > 0 ? 1u : 0u);
-      }
-      umma_commit(bar_mma);
-    }
-    __syncwarp();
-    mbar_wait(bar_mma, mph, status, DEV_TIMEOUT_MMA);
-    __syncwarp();
-    mph ^= 1;
-    tc_fence_after();
-    {
-      uint32_t orr[32];
-      tmem_ld32(tmem_addr(tO, warp * 32, 0), orr);
-      tmem_ld_wait();
-#pragma unroll
-      for (int d = 0; d < C_HEAD; ++d) o[d] += __uint_as_float(orr[d]);
-    }
-    tc_fence_before();
-    // stage s is free (both MMAs that read it are complete): prefetch tile kt + 2
-    if (tid == 0 && kt + 2 < NT) {
-      mbar_arrive_expect_tx(bar_kv + s, 16384);
-      bulk_g2s(sK[s], kimg + (size_t)(kt + 2) * 8192, 8192, bar_kv + s);
-      bulk_g2s(sV[s], vimg + (size_t)(kt + 2) * 8192, 8192, bar_kv + s);
-    }
-  }
-
-  // ---- epilogue: o / l * sigmoid(g) -> core operand image (tile (b, a, qt), channels h*32..) ----
   {
-    const float inv_l = 1.0f / l;
-    const T* g = reinterpret_cast<const T*>(args.ws + args.wl.off_g) + (((size_t)b * R + al) * N + qc) * C_IN + h * C_HEAD;
-    unsigned char* cimg = args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + qt) * 32768;
+    // ================================ softmax warpgroups ================================
+    const int j = warp >> 2, quad = warp & 3;  // row of the group, TMEM lane quadrant
+    const int t = quad * 32 + lane;            // query within the tile = TMEM lane
+    const bool leader = (quad == 0 && lane == 0);
+    const uint32_t buf = tbase + ((uint32_t)(quad * 32) << 16) + j * 128;
+    const uint32_t buf0 = tbase + j * 128;  // lane 0 of the row's columns (MMA operands)
+    constexpr uint32_t idS = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
+    constexpr uint32_t idPV = make_idesc_f16(128, 48, 0, 0, 1);  // fp16 P (TMEM) x fp16 V (MN-major), N = 32 + 16
+    float o[C_HEAD], l = 0.f, m = 0.f;
+    bool started = false;
+    int n = 0;  // tiles processed by this row
 #pragma unroll
-    for (int d = 0; d < C_HEAD; d += 8) {
-      const uint4 gv = *reinterpret_cast<const uint4*>(g + d);
-      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-      uint32_t ow[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 gg = H16<T>::unpack(gw[i]);
-        const float y0 = o[d + 2 * i] * inv_l / (1.0f + __expf(-gg.x));
-        const float y1 = o[d + 2 * i + 1] * inv_l / (1.0f + __expf(-gg.y));
-        ow[i] = valid ? H16<T>::pack(y0, y1) : 0u;
+    for (int d = 0; d < C_HEAD; ++d) o[d] = 0.f;
+    const bool row_ok = g0 + j < R;
+    const size_t tile0 = (head0 + (size_t)(g0 + j) * HEADS) * NT;
+    auto next_active = [&](int kt) {
+      while (kt < NT && scls[j * TILE + kt] != 0 && scls[j * TILE + kt] != 2) ++kt;
+      return kt;
+    };
+    if (leader && row_ok) {
+      mbar_arrive_expect_tx(bar + B_QF + j, 8192);
+      bulk_g2s(smem + CG_SQ + j * 8192, args.ws + args.wl.off_q + (tile0 + qt) * 8192, 8192, bar + B_QF + j);
+      const int k0 = next_active(0);
+      if (k0 < NT) {
+        mbar_arrive_expect_tx(bar + B_KF + j, 8192);
+        bulk_g2s(smem + CG_SK + j * 8192, args.ws + args.wl.off_k + (tile0 + k0) * 8192, 8192, bar + B_KF + j);
+        mbar_arrive_expect_tx(bar + B_VF + j, 8192);
+        bulk_g2s(smem + CG_SV + j * 12288, args.ws + args.wl.off_v + (tile0 + k0) * 8192, 8192, bar + B_VF + j);
       }
-      *reinterpret_cast<uint4*>(cimg + img_off(tid, h * C_HEAD + d, HC)) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      mbar_wait(bar + B_QF + j, 0, status, DEV_TIMEOUT_TMA);
+    }
+
+    // this warp is done reading tri-bias stage kt & 1; the last of the 16 warps refills it with kt + 2
+    auto release_bias = [&](int kt) {
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        const int bs = kt & 1;
+        if (atomicAdd(bias_cnt + bs, 1) == CG_SOFTMAX_WARPS - 1) {
+          bias_cnt[bs] = 0;
+          if (kt + 2 < NT) {
+            fence_proxy_async_smem();
+            load_bias(kt + 2);
+          }
+        }
+      }
+      __syncwarp();
+    };
+    for (int kt = 0; kt < NT; ++kt) {
+      const int bs = kt & 1;
+      const int cls = scls[j * TILE + kt];
+      const bool act = cls == 0 || cls == 2;
+      float alpha = 1.f;
+      if (act) {
+        // S = Q K^T, issued by this row's leader
+        if (leader) {
+          mbar_wait(bar + B_KF + j, n & 1, status, DEV_TIMEOUT_TMA);
+          tc_fence_after();
+#pragma unroll
+          for (int k2 = 0; k2 < C_HEAD / 16; ++k2) {
+            const uint64_t ad = smem_desc_noswizzle(smem_u32(smem + CG_SQ + j * 8192) + k2 * 256, 128, 512);
+            const uint64_t bd = smem_desc_noswizzle(smem_u32(smem + CG_SK + j * 8192) + k2 * 256, 128, 512);
+            umma_ss(buf0, ad, bd, idS, k2 > 0 ? 1u : 0u);
+          }
+          umma_commit(bar + B_SF + j);
+        }
+      }
+      mbar_wait(bar + B_BF + bs, (kt >> 1) & 1, status, DEV_TIMEOUT_TMA);
+      if (act) {
+        mbar_wait(bar + B_SF + j, n & 1, status, DEV_TIMEOUT_MMA);
+        __syncwarp();
+        tc_fence_after();
+        if (leader) {  // S has consumed the K slot: prefetch the row's next key tile
+          const int kn = next_active(kt + 1);
+          if (kn < NT) {
+            mbar_arrive_expect_tx(bar + B_KF + j, 8192);
+            bulk_g2s(smem + CG_SK + j * 8192, args.ws + args.wl.off_k + (tile0 + kn) * 8192, 8192, bar + B_KF + j);
+          }
+        }
+        const unsigned char* tbp = smem + CG_SB + bs * 32768 + t * 16;
+        const float* mbp = reinterpret_cast<const float*>(smem + CG_SMB + (bs * CG_RG + j) * 512);
+        // pass 1: x = S (+ mask bias) + tri bias, row max; x written back over S
+        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sr[32];
+          tmem_ld32(buf + 32 * c, sr);
+          uint4 bw[4];
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) bw[gq] = *reinterpret_cast<const uint4*>(tbp + (4 * c + gq) * 2048);
+          tmem_ld_wait();
+          float xs[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) xs[i] = __uint_as_float(sr[i]);
+          if (cls == 2) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 mv = *reinterpret_cast<const float4*>(mbp + 32 * c + i);
+              xs[i] += mv.x; xs[i + 1] += mv.y; xs[i + 2] += mv.z; xs[i + 3] += mv.w;
+            }
+          }
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) {
+            add_f16_pair(xs[8 * gq + 0], xs[8 * gq + 1], bw[gq].x);
+            add_f16_pair(xs[8 * gq + 2], xs[8 * gq + 3], bw[gq].y);
+            add_f16_pair(xs[8 * gq + 4], xs[8 * gq + 5], bw[gq].z);
+            add_f16_pair(xs[8 * gq + 6], xs[8 * gq + 7], bw[gq].w);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            mxa = max3f(mxa, xs[i], xs[i + 1]);
+            mxb = max3f(mxb, xs[i + 2], xs[i + 3]);
+            mxc = max3f(mxc, xs[i + 4], xs[i + 5]);
+            mxd = max3f(mxd, xs[i + 6], xs[i + 7]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sr[i] = __float_as_uint(xs[i]);
+          tmem_st32(buf + 32 * c, sr);
+        }
+        tmem_st_wait();
+        release_bias(kt);
+        const float mx = fmaxf(max3f(mxa, mxb, mxc), mxd);
+        // lazy rescale: keep the running maximum unless it grew by more than 8 (a factor 256)
+        if (!started) {
+          m = mx;
+          started = true;
+        } else if (mx > m + 8.0f) {
+          alpha = ex2(m - mx);
+          m = mx;
+        }
+        const uint32_t nm = __float_as_uint(-m);
+        const uint64_t neg_m2 = ((uint64_t)nm << 32) | nm;
+        // pass 2: P = 2^(x - m) as fp16 pairs into columns [0, 64)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t xr[32];
+          tmem_ld32(buf + 32 * c, xr);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = exp2_pair_f16(__uint_as_float(xr[2 * i]), __uint_as_float(xr[2 * i + 1]), neg_m2);
+          tmem_st16(buf + 16 * c, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        wg_sync(j);  // every warp of the row has stored its P
+        if (leader) {
+          tc_fence_after();
+          mbar_wait(bar + B_VF + j, n & 1, status, DEV_TIMEOUT_TMA);
+#pragma unroll
+          for (int i = 0; i < TILE / 16; ++i) {
+            const uint64_t bd = smem_desc_noswizzle(smem_u32(smem + CG_SV + j * 12288) + i * 256, 128, 2048);
+            umma_ts(buf0 + 64, buf0 + i * 8, bd, idPV, i > 0 ? 1u : 0u);
+          }
+          umma_commit(bar + B_OF + j);
+        }
+      } else {
+        release_bias(kt);
+      }
+      if (act) {
+        mbar_wait(bar + B_OF + j, n & 1, status, DEV_TIMEOUT_MMA);
+        __syncwarp();
+        tc_fence_after();
+        if (leader) {  // P.V has consumed the V slot: prefetch the row's next value tile
+          const int kn = next_active(kt + 1);
+          if (kn < NT) {
+            mbar_arrive_expect_tx(bar + B_VF + j, 8192);
+            bulk_g2s(smem + CG_SV + j * 12288, args.ws + args.wl.off_v + (tile0 + kn) * 8192, 8192, bar + B_VF + j);
+          }
+        }
+        uint32_t ov[32], lv[16];
+        tmem_ld32(buf + 64, ov);
+        tmem_ld16(buf + 96, lv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int d = 0; d < C_HEAD; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(ov[d]));
+        l = fmaf(l, alpha, __uint_as_float(lv[0]));
+        tc_fence_before();
+        wg_sync(j);  // the row's columns are free for the next S
+        ++n;
+      }
+    }
+
+    // ---- epilogue: o / l * sigmoid(g) -> core operand image of (b, row, qt), channels h*32.. ----
+    if (row_ok) {
+      const int q = qt * TILE + t;
+      const bool qvalid = q < N;
+      const int qc = qvalid ? q : N - 1;
+      const int al = g0 + j;
+      const float inv_l = 1.0f / l;
+      const T* g = reinterpret_cast<const T*>(args.ws + args.wl.off_g) + (((size_t)b * R + al) * N + qc) * C_IN + h * C_HEAD;
+      unsigned char* cimg = args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + qt) * 32768;
+#pragma unroll
+      for (int d = 0; d < C_HEAD; d += 8) {
+        const uint4 gv = *reinterpret_cast<const uint4*>(g + d);
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 gg = H16<T>::unpack(gw[i]);
+          const float y0 = o[d + 2 * i] * inv_l / (1.0f + __expf(-gg.x));
+          const float y1 = o[d + 2 * i + 1] * inv_l / (1.0f + __expf(-gg.y));
+          ow[i] = qvalid ? H16<T>::pack(y0, y1) : 0u;
+        }
+        *reinterpret_cast<uint4*>(cimg + img_off(t, h * C_HEAD + d, HC)) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
     }
   }
+
+  tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 256);
+  if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
 template <typename T>
 static cudaError_t core_tc_launch(const LayerArgs& a, cudaStream_t st) {
-  // at least ~100 KB of shared memory per CTA: two CTAs per SM, matching the 2 x 256 TMEM columns
-  const int smem = max(CORE_SMEM_FIXED + a.wl.Np * 4, 100 * 1024);
-  cudaFuncSetAttribute(core_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(core_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, CG_SMEM);
   const int R = a.row_end - a.row_begin;
-  dim3 grid(a.wl.NT, R, a.B * HEADS);
-  core_tc_kernel<T><<<grid, 128, smem, st>>>(a);
+  dim3 grid(a.wl.NT, (R + CG_RG - 1) / CG_RG, a.B * HEADS);
+  core_tc_kernel<T><<<grid, CG_THREADS, CG_SMEM, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -14,6 +14,7 @@ constexpr int HC = HEADS * C_HEAD;  // 128
 constexpr int NPROJ = 4 * HC;       // 512 = q|k|v|g
 constexpr float LN_EPS = 1e-5f;
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr float QSCALE_L2 = 0.17677669529663687f * 1.4426950408889634f;  // C^-1/2 * log2(e)
 constexpr int TILE = 128;  // query / key / pair tile of the tensor-core path
 
 constexpr int DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2;
@@ -41,19 +42,24 @@ struct PackedLayout {
 // ---- workspace ---------------------------------------------------------------------------------
 // The tri-bias region comes first, at offset 0, so it sits at the same place whatever row count a
 // call is made with: row chunks of different sizes (and the ranks of a row-sharded layer) fill and
-// read one shared [N][B][H][Np] bias.  Per-row regions follow, laid out for R = row_end - row_begin.
-//   bias                : [N][B][H][Np] fp32 tri bias of ALL N query rows (log2 domain on the 16-bit
-//                         path, natural units on the fp32 path)
+// read one shared bias.  Per-row regions follow, laid out for R = row_end - row_begin.
 // 16-bit path (NT = Np / 128 tiles, Np = N rounded up to 128):
-//   q_img, k_img, v_img : [B][R][H][NT] tiles of 8 KB (128 positions x 32 channels operand image)
-//   g                   : [B][R][N][128] 16-bit
-//   core_img            : [B][R][NT] tiles of 32 KB (128 positions x 128 channels operand image)
-//   mb                  : [B][R][Np] fp32, log2-domain mask bias; padded keys -1e30
+//   bias     : fp16, log2 domain, 128 x 128 blocks [qt][b][h][kt], each block stored [k/8][q][8]
+//              (a query's 8 consecutive keys are 16 contiguous bytes; 2 KB between key groups)
+//   q_img    : [B][R][H][NT] tiles of 8 KB, K-major 128 x 32 image, q pre-scaled by C^-1/2 log2(e)
+//   k_img    : [B][R][H][NT] tiles of 8 KB, K-major 128 x 32 image
+//   v_img    : [B][R][H][NT] tiles of 8 KB, fp16, MN-major image: byte(key, ch) =
+//              (ch/8)*2048 + (key/8)*128 + (key%8)*16 + (ch%8)*2
+//   g        : [B][R][N][128] 16-bit
+//   core_img : [B][R][NT] tiles of 32 KB (128 positions x 128 channels, K-major image)
+//   mb       : [B][R][Np] fp32, log2-domain mask bias; padded keys -1e30
+//   ts       : [B][R][NT] uint8 key-tile class: 0 all keys valid, 1 all masked (skip), 2 mixed
 // fp32 path:
+//   bias     : [N][B][H][Np] fp32 tri bias (natural units)
 //   q (pre-scaled by C^-1/2), k, v, g, core : [B][R][N][128] fp32;  mb : [B][R][Np] = inf * (mask - 1)
 struct Workspace {
   int B, N, R, dtype, Np, NT;
-  size_t off_q, off_k, off_v, off_g, off_core, off_bias, off_mb, total;
+  size_t off_q, off_k, off_v, off_g, off_core, off_bias, off_mb, off_ts, total;
 
   __host__ __device__ static Workspace make(int B, int N, int R, int dtype) {
     Workspace w{};
@@ -62,7 +68,8 @@ struct Workspace {
     w.NT = w.Np / TILE;
     const size_t A = 256;
     size_t o = 0;
-    w.off_bias = o; o = align_up(o + (size_t)N * B * HEADS * w.Np * 4, A);
+    w.off_bias = o;
+    o = align_up(o + (dtype == DT_F32 ? (size_t)N * B * HEADS * w.Np * 4 : (size_t)w.Np * B * HEADS * w.Np * 2), A);
     if (dtype == DT_F32) {
       const size_t plane = (size_t)B * R * N * C_IN * 4;
       w.off_q = o; o = align_up(o + plane, A);
@@ -79,10 +86,22 @@ struct Workspace {
       w.off_core = o; o = align_up(o + (size_t)B * R * w.NT * 32768, A);
     }
     w.off_mb = o; o = align_up(o + (size_t)B * R * w.Np * 4, A);
+    w.off_ts = o; o = align_up(o + (size_t)B * R * w.NT, A);
     w.total = o;
     return w;
   }
 };
+
+// Byte offset of tri-bias element (q, k) of head h, batch b on the 16-bit path.
+__host__ __device__ __forceinline__ size_t bias16_off(int q, int k, int b, int h, int B, int NT) {
+  const size_t blk = (((size_t)(q >> 7) * B + b) * HEADS + h) * NT + (k >> 7);
+  return blk * 32768 + (size_t)((k & 127) >> 3) * 2048 + (size_t)(q & 127) * 16 + (k & 7) * 2;
+}
+
+// Byte offset of V element (key, ch) inside a 128-key x 32-channel fp16 V image (MN-major).
+__host__ __device__ __forceinline__ uint32_t vimg_off(uint32_t key, uint32_t ch) {
+  return (ch >> 3) * 2048u + (key >> 3) * 128u + (key & 7u) * 16u + (ch & 7u) * 2u;
+}
 
 // Attention-oriented view of a [B][N][N][ch] tensor: element (b, a, c, ch) lives at
 //   base + b * s_batch + (a - row0) * s_row + c * s_col + ch
@@ -110,6 +129,7 @@ cudaError_t launch_pack_weights(const float* ln_w, const float* ln_b, const floa
                                 const float* w_v, const float* w_g, const float* g_bias, const float* w_b,
                                 const float* w_o, int dtype, unsigned char* packed, cudaStream_t st);
 cudaError_t launch_mask_prep(const LayerArgs& a, int dtype, cudaStream_t st);
+cudaError_t launch_mask_prep_tc(const LayerArgs& a, cudaStream_t st);
 cudaError_t launch_ln_proj_f32(const LayerArgs& a, cudaStream_t st);
 cudaError_t launch_core_f32(const LayerArgs& a, cudaStream_t st);
 cudaError_t launch_out_proj_f32(const LayerArgs& a, cudaStream_t st);

@@ -72,6 +72,9 @@ class ShardedPair:
         self.r0, self.r1 = shard_rows(N, self.P, self.rank)
         self.R = self.r1 - self.r0
         self.dt = _lib.dtype_code(precision)
+        if self.dt != _lib.F32 and self.R % 128:
+            raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED,
+                                          f"16-bit row sharding needs rows per rank ({self.R}) to be a multiple of 128")
         self.w = Workspace.make(1, N, self.R, self.dt)
         self.ws = torch.empty(self.w.total, dtype=torch.uint8, device=device)
         self.send = torch.empty(self.P, self.R, self.R, C_IN, device=device)

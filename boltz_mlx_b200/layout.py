@@ -52,6 +52,7 @@ class Workspace:
     off_core: int = 0
     off_bias: int = 0
     off_mb: int = 0
+    off_ts: int = 0
     total: int = 0
 
     @classmethod
@@ -61,7 +62,8 @@ class Workspace:
         w.NT = w.Np // TILE
         o = 0
         # tri bias first: one fixed place for every row count (row chunks / ranks share it)
-        w.off_bias = o; o = align(o + N * B * HEADS * w.Np * 4)
+        w.off_bias = o
+        o = align(o + (N * B * HEADS * w.Np * 4 if dtype == F32 else w.Np * B * HEADS * w.Np * 2))
         if dtype == F32:
             plane = B * R * N * C_IN * 4
             w.off_q = o; o = align(o + plane)
@@ -77,17 +79,64 @@ class Workspace:
             w.off_g = o; o = align(o + B * R * N * C_IN * 2)
             w.off_core = o; o = align(o + B * R * w.NT * 32768)
         w.off_mb = o; o = align(o + B * R * w.Np * 4)
+        w.off_ts = o; o = align(o + B * R * w.NT)
         w.total = o
         return w
 
-    # byte range of the tri-bias rows [r0, r1) (layout [N][B][H][Np] fp32): contiguous per row block
+    # byte range of the tri-bias rows [r0, r1): contiguous per row block.  fp32 path: layout
+    # [N][B][H][Np] fp32.  16-bit path: 128-row blocks [qt][b][h][kt] (fp16), so r0 and r1 must be
+    # multiples of 128 (or r1 = N for the last block).
     def bias_rows(self, r0: int, r1: int) -> tuple[int, int]:
-        row = self.B * HEADS * self.Np * 4
-        return self.off_bias + r0 * row, self.off_bias + r1 * row
+        if self.dtype == F32:
+            row = self.B * HEADS * self.Np * 4
+            return self.off_bias + r0 * row, self.off_bias + r1 * row
+        if r0 % TILE or (r1 % TILE and r1 != self.N):
+            raise ValueError(f"16-bit tri-bias rows move in blocks of {TILE} rows: [{r0}, {r1})")
+        row = self.B * HEADS * self.Np * 2
+        return self.off_bias + r0 * row, self.off_bias + round_tile(r1) * row
 
 
 def workspace_bytes(B: int, N: int, rows: int, dtype: int) -> int:
     return Workspace.make(B, N, rows, dtype).total
+
+
+def bias16_offsets(N: int, B: int, NT: int):
+    """Byte offsets [B, H, N(q), N(k)] of the 16-bit tri-bias blocks."""
+    q = np.arange(N)[:, None]
+    k = np.arange(N)[None, :]
+    out = np.empty((B, HEADS, N, N), np.int64)
+    for b in range(B):
+        for h in range(HEADS):
+            blk = (((q >> 7) * B + b) * HEADS + h) * NT + (k >> 7)
+            out[b, h] = blk * 32768 + ((k & 127) >> 3) * 2048 + (q & 127) * 16 + (k & 7) * 2
+    return out
+
+
+def vimg_offsets() -> np.ndarray:
+    """Byte offset of (key, ch) inside a 128 x 32 fp16 V image (MN-major), shape [128, 32]."""
+    key = np.arange(TILE)[:, None]
+    ch = np.arange(C_HEAD)[None, :]
+    return (ch >> 3) * 2048 + (key >> 3) * 128 + (key & 7) * 16 + (ch & 7) * 2
+
+
+def decode_v_images(buf, w: "Workspace"):
+    """v images -> tensor [B, R, H, Np, 32] (fp16 values as float32)."""
+    import torch
+
+    n = w.B * w.R * HEADS * w.NT * 8192
+    raw = buf[w.off_v:w.off_v + n].view(torch.float16).view(w.B, w.R, HEADS, w.NT, 4096)
+    idx = torch.from_numpy(vimg_offsets() // 2).to(buf.device)
+    return raw[..., idx].float().reshape(w.B, w.R, HEADS, w.Np, C_HEAD)
+
+
+def decode_bias16(buf, w: "Workspace"):
+    """16-bit tri bias -> tensor [B, H, N(q), N(k)] (log2 domain, float32)."""
+    import torch
+
+    n = w.Np * w.B * HEADS * w.Np * 2
+    raw = buf[w.off_bias:w.off_bias + n].view(torch.float16)
+    idx = torch.from_numpy(bias16_offsets(w.N, w.B, w.NT) // 2).to(buf.device)
+    return raw[idx].float()
 
 
 def decode_head_images(buf, w: Workspace, off: int):

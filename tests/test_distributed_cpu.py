@@ -45,6 +45,8 @@ def _worker(rank, P, port, N, errq):
         assert torch.equal(out, ref[r0:r1]), "cols_to_rows"
         # tri-bias all-gather over the workspace layout
         for dtype in (0, 2):
+            if dtype != 0 and R % 128:
+                continue  # 16-bit tri-bias rows move in 128-row blocks
             w = Workspace.make(1, N, R, dtype)
             ws = torch.zeros(w.total, dtype=torch.uint8)
             l0, l1 = w.bias_rows(r0, r1)

@@ -11,6 +11,7 @@ from tests._util import module, rand_mask
 
 pytestmark = pytest.mark.gpu
 LOG2E = 1.4426950408889634
+QSCALE_L2 = C_HEAD ** -0.5 * LOG2E  # q is stored pre-scaled: S = q.k comes out in log2 units
 
 
 def t16(precision):
@@ -59,38 +60,65 @@ def test_ln_proj_stage(precision, N, starting):
     xn, h, tb = ref_projection(ctx, precision)
     # a 16-bit ulp: accumulation order and 1-ulp LN differences flip the last rounding of a few values
     ulp = 2.0 ** -8 if precision == "bf16" else 2.0 ** -11
-    for i, off in enumerate((w.off_q, w.off_k, w.off_v)):
+    f16ulp = 2.0 ** -11
+    for i, off in enumerate((w.off_q, w.off_k)):
         img = layout.decode_head_images(ws, w, off).cpu()  # [B, R, H, Np, 32]
         ref = h[..., i * HC:(i + 1) * HC].reshape(B, N, N, HEADS, C_HEAD).permute(0, 1, 3, 2, 4)
+        if i == 0:
+            ref = ref * QSCALE_L2
         got = img[:, :, :, :N]
         torch.testing.assert_close(got, ref.to(t16(precision)).float(), rtol=2 * ulp,
                                    atol=ulp * float(ref.abs().max()), msg=lambda m: f"image {i}: {m}")
         assert torch.all(img[:, :, :, N:] == 0), "padded positions must be zero"
+    vimg = layout.decode_v_images(ws, w).cpu()
+    vref = h[..., 2 * HC:3 * HC].reshape(B, N, N, HEADS, C_HEAD).permute(0, 1, 3, 2, 4)
+    # V is fp16 in every 16-bit mode; its operand is the bf16/fp16-rounded xn, so compare at that ulp
+    torch.testing.assert_close(vimg[:, :, :, :N], vref.half().float(), rtol=2 * max(ulp, f16ulp),
+                               atol=ulp * float(vref.abs().max()))
+    assert torch.all(vimg[:, :, :, N:] == 0)
     gbuf = ws[w.off_g:w.off_g + B * N * N * 128 * 2].view(t16(precision)).view(B, N, N, 128).float().cpu()
     gref = (h[..., 3 * HC:] + 1.0).to(t16(precision)).float()
     torch.testing.assert_close(gbuf, gref, rtol=2 * ulp, atol=ulp * float(gref.abs().max()))
-    bias = ws[w.off_bias:w.off_bias + N * B * HEADS * w.Np * 4].view(torch.float32).view(N, B, HEADS, w.Np).cpu()
-    ref_b = (tb * LOG2E).permute(1, 0, 3, 2)  # [q=a][b][h][k=c]
-    torch.testing.assert_close(bias[..., :N], ref_b, rtol=1e-4, atol=1e-5)
-    assert torch.all(bias[..., N:] == 0)
+    bias = layout.decode_bias16(ws, w).cpu()  # [B, H, q, k]
+    ref_b = (tb * LOG2E).permute(0, 3, 1, 2)  # tb [B, q, k, H]
+    torch.testing.assert_close(bias, ref_b.half().float(), rtol=2 * f16ulp, atol=1e-4)
 
 
 def ref_core(ctx, precision):
-    """Softmax attention on the decoded 16-bit q/k/v/g images, fp32, log2 domain (kernels_nax.py:376-406)."""
+    """Softmax attention on the decoded operand images, fp32, log2 domain (kernels_nax.py:376-406):
+    S = q'.k (q' pre-scaled), x = S + mask bias + tri bias, p = 2^(x - max), o = p v / sum p, * sigmoid(g)."""
     w, ws, B, N = ctx["w"], ctx["ws"], ctx["B"], ctx["N"]
     q = layout.decode_head_images(ws, w, w.off_q)[:, :, :, :N].cpu()
     k = layout.decode_head_images(ws, w, w.off_k)[:, :, :, :N].cpu()
-    v = layout.decode_head_images(ws, w, w.off_v)[:, :, :, :N].cpu()
+    v = layout.decode_v_images(ws, w)[:, :, :, :N].cpu()
     g = ws[w.off_g:w.off_g + B * N * N * 128 * 2].view(t16(precision)).view(B, N, N, 128).float().cpu()
-    bias = ws[w.off_bias:w.off_bias + N * B * HEADS * w.Np * 4].view(torch.float32).view(N, B, HEADS, w.Np).cpu()
+    bias = layout.decode_bias16(ws, w).cpu()  # [B, H, q, k]
     mb = ws[w.off_mb:w.off_mb + B * N * w.Np * 4].view(torch.float32).view(B, N, w.Np).cpu()
-    s = torch.einsum("bahqd,bahkd->bahqk", q, k) * (C_HEAD ** -0.5 * LOG2E)
-    s = s + mb[:, :, None, None, :N] + bias[..., :N].permute(1, 2, 0, 3)[:, None]
+    s = torch.einsum("bahqd,bahkd->bahqk", q, k)
+    s = (s + mb[:, :, None, None, :N]) + bias[:, None]
     s = s - s.amax(-1, keepdim=True)
     pr = torch.exp2(s)
     o = torch.einsum("bahqk,bahkd->bahqd", pr, v) / pr.sum(-1, keepdim=True)
     o = o.permute(0, 1, 3, 2, 4).reshape(B, N, N, HC)
     return o * torch.sigmoid(g)
+
+
+def test_tile_classes():
+    """Key-tile classes: 0 all valid, 1 all masked with valid keys elsewhere (skipped), 2 mixed or a
+    row without any valid key (kept, so it attends uniformly)."""
+    N = 300
+    mask = torch.ones(1, N, N)
+    mask[0, 0, 128:256] = 0  # row 0: tile 1 fully masked -> skipped
+    mask[0, 1, 5] = 0  # row 1: tile 0 mixed
+    mask[0, 2, :] = 0  # row 2: no valid key -> every tile kept
+    ctx = run_ln_proj(N, "bf16", True, mask=mask)
+    w, ws = ctx["w"], ctx["ws"]
+    ts = ws[w.off_ts:w.off_ts + N * w.NT].view(N, w.NT).cpu().tolist()
+    assert w.NT == 3
+    assert ts[0] == [0, 1, 2]  # the last tile holds padded keys -> mixed
+    assert ts[1] == [2, 0, 2]
+    assert ts[2] == [2, 2, 2]
+    assert ts[3] == [0, 0, 2]
 
 
 @pytest.mark.parametrize("precision", ["bf16", "fp16"])
