@@ -295,19 +295,20 @@ cudaError_t launch_mask_prep_tc(const LayerArgs& a, cudaStream_t st) {
 constexpr int CG_RG = 4;
 constexpr int CG_SOFTMAX_WARPS = 4 * CG_RG;
 constexpr int CG_THREADS = CG_SOFTMAX_WARPS * 32;
+constexpr int CG_NB = 3;                           // tri-bias stages
 constexpr int CG_SQ = 0;                           // RG Q tiles, 8 KB each
-constexpr int CG_SB = CG_SQ + CG_RG * 8192;        // 2 tri-bias stages, 32 KB each (fp16)
-constexpr int CG_SMB = CG_SB + 2 * 32768;          // 2 stages x RG mask-bias slices of 512 B
-constexpr int CG_SK = CG_SMB + 2 * CG_RG * 512;    // one K slot per row, 8 KB
+constexpr int CG_SB = CG_SQ + CG_RG * 8192;        // NB tri-bias stages, 32 KB each (fp16)
+constexpr int CG_SMB = CG_SB + CG_NB * 32768;      // NB stages x RG mask-bias slices of 512 B
+constexpr int CG_SK = CG_SMB + CG_NB * CG_RG * 512;  // one K slot per row, 8 KB
 constexpr int CG_SV = CG_SK + CG_RG * 8192;        // one V slot per row, 12 KB (8 KB V + 4 KB ones/zeros)
 constexpr int CG_BAR = CG_SV + CG_RG * 12288;
 constexpr int CG_CLS = CG_BAR + 512;               // RG x 128 key-tile classes
-constexpr int CG_CNT = CG_CLS + CG_RG * TILE;      // 2 tri-bias stage arrival counters
+constexpr int CG_CNT = CG_CLS + CG_RG * TILE;      // NB tri-bias stage arrival counters
 constexpr int CG_SMEM = CG_CNT + 16;
 static_assert(CG_SMEM <= 232448, "core shared memory");
 
 // barrier slots
-constexpr int B_BF = 0, B_QF = 2, B_KF = B_QF + CG_RG, B_VF = B_KF + CG_RG, B_SF = B_VF + CG_RG,
+constexpr int B_BF = 0, B_QF = CG_NB, B_KF = B_QF + CG_RG, B_VF = B_KF + CG_RG, B_SF = B_VF + CG_RG,
               B_OF = B_SF + CG_RG, B_COUNT = B_OF + CG_RG;
 static_assert(B_COUNT * 8 + 16 <= 512, "barrier area");
 
@@ -337,6 +338,44 @@ __device__ __forceinline__ uint32_t exp2_pair_f16(float x0, float x1, uint64_t n
   return r;
 }
 
+// 2^(x0 - m), 2^(x1 - m) as an fp16 pair computed without the MUFU (FMA and ALU pipes only), so a
+// share of the exponentials runs beside the MUFU ones.  Cody-Waite style split: y = max(x - m, -32),
+// n = round(y) with the 1.5 * 2^23 shifter, f = y - n in [-0.5, 0.5], 2^f from a degree-3
+// polynomial fitted to 2^f on [-0.5, 0.5] by iteratively reweighted least squares on the relative
+// error (max relative error 7.5e-5, below the fp16 rounding of P), then 2^y = 2^f * 2^n by adding
+// n to the exponent field.
+__device__ __forceinline__ uint32_t exp2_pair_poly_f16(float x0, float x1, uint64_t neg_m2) {
+  constexpr float kC0 = 0x1.fff696p-1f, kC1 = 0x1.62f31ap-1f, kC2 = 0x1.f0dd6ep-3f, kC3 = 0x1.c3f60cp-5f;
+  const uint64_t sh2 = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
+  const uint64_t c3 = ((uint64_t)__float_as_uint(kC3) << 32) | __float_as_uint(kC3);
+  const uint64_t c2 = ((uint64_t)__float_as_uint(kC2) << 32) | __float_as_uint(kC2);
+  const uint64_t c1 = ((uint64_t)__float_as_uint(kC1) << 32) | __float_as_uint(kC1);
+  const uint64_t c0 = ((uint64_t)__float_as_uint(kC0) << 32) | __float_as_uint(kC0);
+  float y0, y1;
+  asm("{\n\t.reg .b64 d;\n\tmov.b64 d, {%2, %3};\n\tadd.rn.f32x2 d, d, %4;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(y0), "=f"(y1)
+      : "f"(x0), "f"(x1), "l"(neg_m2));
+  y0 = fmaxf(y0, -32.0f);
+  y1 = fmaxf(y1, -32.0f);
+  uint32_t t0, t1, p0, p1;
+  asm("{\n\t.reg .b64 y, t, n, f, p;\n\t"
+      "mov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 t, y, %6;\n\t"
+      "sub.rn.f32x2 n, t, %6;\n\t"
+      "sub.rn.f32x2 f, y, n;\n\t"
+      "fma.rn.f32x2 p, %7, f, %8;\n\t"
+      "fma.rn.f32x2 p, p, f, %9;\n\t"
+      "fma.rn.f32x2 p, p, f, %10;\n\t"
+      "mov.b64 {%0, %1}, t;\n\tmov.b64 {%2, %3}, p;\n\t}"
+      : "=r"(t0), "=r"(t1), "=r"(p0), "=r"(p1)
+      : "f"(y0), "f"(y1), "l"(sh2), "l"(c3), "l"(c2), "l"(c1), "l"(c0));
+  const float e0 = __uint_as_float(p0 + (t0 << 23));
+  const float e1 = __uint_as_float(p1 + (t1 << 23));
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(e1), "f"(e0));
+  return r;
+}
+
 // Named barrier of one softmax warpgroup (ids 1..RG; 0 is __syncthreads).
 __device__ __forceinline__ void wg_sync(int j) { asm volatile("bar.sync %0, 128;" ::"r"(j + 1) : "memory"); }
 
@@ -356,7 +395,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
   // ---- set-up: barriers, V-slot tails, key-tile classes, TMEM ----
   int* bias_cnt = reinterpret_cast<int*>(smem + CG_CNT);
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) mbar_init(bar + B_BF + i, 1);
+    for (int i = 0; i < CG_NB; ++i) mbar_init(bar + B_BF + i, 1);
     for (int j = 0; j < CG_RG; ++j) {
       mbar_init(bar + B_QF + j, 1);
       mbar_init(bar + B_KF + j, 1);
@@ -364,7 +403,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
       mbar_init(bar + B_SF + j, 1);
       mbar_init(bar + B_OF + j, 1);
     }
-    bias_cnt[0] = bias_cnt[1] = 0;
+    for (int i = 0; i < CG_NB; ++i) bias_cnt[i] = 0;
     fence_mbar_init();
   }
   // V slot tail: channel group 4 = (1, 0, ..., 0) per key (the ones column that yields the row
@@ -391,9 +430,9 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
   for (int jj = 0; jj < CG_RG; ++jj) nrow += (g0 + jj < R);
   const unsigned char* bias_blk = args.ws + args.wl.off_bias + (((size_t)qt * args.B + b) * HEADS + h) * NT * 32768;
   const float* mb_all = reinterpret_cast<const float*>(args.ws + args.wl.off_mb);
-  // tri-bias tile kt (+ the mask-bias slices of the group's rows) -> stage kt & 1
+  // tri-bias tile kt (+ the mask-bias slices of the group's rows) -> stage kt % NB
   auto load_bias = [&](int kt) {
-    const int bs = kt & 1;
+    const int bs = kt % CG_NB;
     mbar_arrive_expect_tx(bar + B_BF + bs, 32768 + nrow * 512);
     bulk_g2s(smem + CG_SB + bs * 32768, bias_blk + (size_t)kt * 32768, 32768, bar + B_BF + bs);
     for (int jj = 0; jj < CG_RG; ++jj)
@@ -401,10 +440,8 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
         bulk_g2s(smem + CG_SMB + (bs * CG_RG + jj) * 512, mb_all + ((size_t)b * R + g0 + jj) * Np + kt * TILE, 512,
                  bar + B_BF + bs);
   };
-  if (tid == 0) {
-    load_bias(0);
-    if (NT > 1) load_bias(1);
-  }
+  if (tid == 0)
+    for (int kt = 0; kt < CG_NB && kt < NT; ++kt) load_bias(kt);
 
   {
     // ================================ softmax warpgroups ================================
@@ -439,24 +476,24 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
       mbar_wait(bar + B_QF + j, 0, status, DEV_TIMEOUT_TMA);
     }
 
-    // this warp is done reading tri-bias stage kt & 1; the last of the 16 warps refills it with kt + 2
+    // this warp is done reading tri-bias stage kt % NB; the last of the 16 warps refills it with kt + NB
     auto release_bias = [&](int kt) {
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
-        const int bs = kt & 1;
+        const int bs = kt % CG_NB;
         if (atomicAdd(bias_cnt + bs, 1) == CG_SOFTMAX_WARPS - 1) {
           bias_cnt[bs] = 0;
-          if (kt + 2 < NT) {
+          if (kt + CG_NB < NT) {
             fence_proxy_async_smem();
-            load_bias(kt + 2);
+            load_bias(kt + CG_NB);
           }
         }
       }
       __syncwarp();
     };
     for (int kt = 0; kt < NT; ++kt) {
-      const int bs = kt & 1;
+      const int bs = kt % CG_NB;
       const int cls = scls[j * TILE + kt];
       const bool act = cls == 0 || cls == 2;
       float alpha = 1.f;
@@ -474,7 +511,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
           umma_commit(bar + B_SF + j);
         }
       }
-      mbar_wait(bar + B_BF + bs, (kt >> 1) & 1, status, DEV_TIMEOUT_TMA);
+      mbar_wait(bar + B_BF + bs, (kt / CG_NB) & 1, status, DEV_TIMEOUT_TMA);
       if (act) {
         mbar_wait(bar + B_SF + j, n & 1, status, DEV_TIMEOUT_MMA);
         __syncwarp();
@@ -546,9 +583,11 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
           tmem_ld32(buf + 32 * c, xr);
           tmem_ld_wait();
           uint32_t pk[16];
+          // 10 of every 16 pairs on the MUFU, 6 on the FMA/ALU pipes (the split that balances the two)
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            pk[i] = exp2_pair_f16(__uint_as_float(xr[2 * i]), __uint_as_float(xr[2 * i + 1]), neg_m2);
+            pk[i] = (i % 8) < 5 ? exp2_pair_f16(__uint_as_float(xr[2 * i]), __uint_as_float(xr[2 * i + 1]), neg_m2)
+                                : exp2_pair_poly_f16(__uint_as_float(xr[2 * i]), __uint_as_float(xr[2 * i + 1]), neg_m2);
           tmem_st16(buf + 16 * c, pk);
         }
         tmem_st_wait();
