@@ -630,27 +630,20 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
       }
     }
 
-    // ---- epilogue: o / l * sigmoid(g) -> core operand image of (b, row, qt), channels h*32.. ----
+    // ---- epilogue: o / l -> fp16 core image of (b, row, qt), channels h*32.. (the sigmoid gate is
+    //      applied by the output projection, which streams the matching g tile) ----
     if (row_ok) {
       const int q = qt * TILE + t;
       const bool qvalid = q < N;
-      const int qc = qvalid ? q : N - 1;
       const int al = g0 + j;
       const float inv_l = 1.0f / l;
-      const T* g = reinterpret_cast<const T*>(args.ws + args.wl.off_g) + (((size_t)b * R + al) * N + qc) * C_IN + h * C_HEAD;
       unsigned char* cimg = args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + qt) * 32768;
 #pragma unroll
       for (int d = 0; d < C_HEAD; d += 8) {
-        const uint4 gv = *reinterpret_cast<const uint4*>(g + d);
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
         uint32_t ow[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 gg = H16<T>::unpack(gw[i]);
-          const float y0 = o[d + 2 * i] * inv_l / (1.0f + __expf(-gg.x));
-          const float y1 = o[d + 2 * i + 1] * inv_l / (1.0f + __expf(-gg.y));
-          ow[i] = qvalid ? H16<T>::pack(y0, y1) : 0u;
-        }
+        for (int i = 0; i < 4; ++i)
+          ow[i] = qvalid ? H16<__half>::pack(o[d + 2 * i] * inv_l, o[d + 2 * i + 1] * inv_l) : 0u;
         *reinterpret_cast<uint4*>(cimg + img_off(t, h * C_HEAD + d, HC)) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     }
@@ -675,7 +668,7 @@ cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 }
 
 // =================================================================================================
-// Output projection (+ residual).  CTA = 128 pairs; y[128 x 128] = core[128 x 128] * W_o^T.
+// Output projection (+ residual).  CTA = 128 pairs; y[128 x 128] = (core o sigmoid(g))[128 x 128] * W_o^T.
 // =================================================================================================
 constexpr int OP_SMEM = 65536 + 64;
 
@@ -704,7 +697,37 @@ __global__ void __launch_bounds__(128) out_proj_tc_kernel(LayerArgs args) {
     mbar_arrive_expect_tx(bars + 0, 65536);
     bulk_g2s(sA, args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + ct) * 32768, 32768, bars + 0);
     bulk_g2s(sW, args.packed + PackedLayout::img_o, 32768, bars + 0);
-    mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
+  }
+  // gate: the fp16 core image row of query ct*128 + tid times sigmoid(g) of the same (b, row, query),
+  // rounded once to T, in place (the MMA then reads a T image)
+  {
+    const int q = min(ct * TILE + tid, N - 1);
+    const uint4* g = reinterpret_cast<const uint4*>(args.ws + args.wl.off_g + (((size_t)b * R + al) * N + q) * C_IN * 2);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint4 gv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gv[i] = __ldcs(g + 8 * half + i);
+      if (half == 0) mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint4* cp = reinterpret_cast<uint4*>(sA + img_off(tid, 8 * (8 * half + i), HC));
+        const uint4 cv = *cp;
+        const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 c2 = H16<__half>::unpack(cw[e]);
+          const float2 g2 = H16<T>::unpack(gw[e]);
+          ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
+        }
+        *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
     tc_fence_after();
     constexpr uint32_t idesc = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
 #pragma unroll

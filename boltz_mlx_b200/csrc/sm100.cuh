@@ -181,6 +181,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 // 16 consecutive 32-bit TMEM columns of this thread's lane -> 16 registers (warp-collective).
+// One 32-bit TMEM column of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t (&r)[1]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -191,6 +196,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Ties registers filled by an earlier tcgen05.ld to the point after tmem_ld_wait(): the compiler then
+// cannot move their uses above the wait (the load's outputs look defined at the load itself).
+template <int NR>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[NR]) {
+#pragma unroll
+  for (int i = 0; i < NR; ++i) asm volatile("" : "+r"(r[i]));
+}
 
 // 32 registers -> 32 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {

@@ -151,11 +151,10 @@ def decode_head_images(buf, w: Workspace, off: int):
 
 
 def decode_core_images(buf, w: Workspace):
-    """core images -> tensor [B, R, Np, 128]."""
+    """core images (fp16 o / l, before the sigmoid gate, for both 16-bit precisions) -> tensor [B, R, Np, 128]."""
     import torch
 
-    tdt = torch.bfloat16 if w.dtype == BF16 else torch.float16
     n = w.B * w.R * w.NT * 32768
-    raw = buf[w.off_core:w.off_core + n].view(tdt).view(w.B, w.R, w.NT, 16384)
+    raw = buf[w.off_core:w.off_core + n].view(torch.float16).view(w.B, w.R, w.NT, 16384)
     idx = torch.from_numpy(img_offsets(TILE, C_IN) // 2).to(buf.device)
     return raw[..., idx].float().reshape(w.B, w.R, w.Np, C_IN)

@@ -86,12 +86,12 @@ def test_ln_proj_stage(precision, N, starting):
 
 def ref_core(ctx, precision):
     """Softmax attention on the decoded operand images, fp32, log2 domain (kernels_nax.py:376-406):
-    S = q'.k (q' pre-scaled), x = S + mask bias + tri bias, p = 2^(x - max), o = p v / sum p, * sigmoid(g)."""
+    S = q'.k (q' pre-scaled), x = S + mask bias + tri bias, p = 2^(x - max), o = p v / sum p (the core
+    stage stores o; the sigmoid gate is applied by the output projection)."""
     w, ws, B, N = ctx["w"], ctx["ws"], ctx["B"], ctx["N"]
     q = layout.decode_head_images(ws, w, w.off_q)[:, :, :, :N].cpu()
     k = layout.decode_head_images(ws, w, w.off_k)[:, :, :, :N].cpu()
     v = layout.decode_v_images(ws, w)[:, :, :, :N].cpu()
-    g = ws[w.off_g:w.off_g + B * N * N * 128 * 2].view(t16(precision)).view(B, N, N, 128).float().cpu()
     bias = layout.decode_bias16(ws, w).cpu()  # [B, H, q, k]
     mb = ws[w.off_mb:w.off_mb + B * N * w.Np * 4].view(torch.float32).view(B, N, w.Np).cpu()
     s = torch.einsum("bahqd,bahkd->bahqk", q, k)
@@ -99,8 +99,7 @@ def ref_core(ctx, precision):
     s = s - s.amax(-1, keepdim=True)
     pr = torch.exp2(s)
     o = torch.einsum("bahqk,bahkd->bahqd", pr, v) / pr.sum(-1, keepdim=True)
-    o = o.permute(0, 1, 3, 2, 4).reshape(B, N, N, HC)
-    return o * torch.sigmoid(g)
+    return o.permute(0, 1, 3, 2, 4).reshape(B, N, N, HC)
 
 
 def test_tile_classes():
@@ -154,10 +153,18 @@ def test_out_proj_stage(precision, starting, residual):
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     core = layout.decode_core_images(ws, w)[:, :, :N].cpu()
+    g = ws[w.off_g:w.off_g + N * N * 128 * 2].view(t16(precision)).view(1, N, N, 128).float().cpu()
+    gated = core * torch.sigmoid(g)  # rounded once to the 16-bit type inside the kernel
     wo = ctx["p"]["w_o"].to(t16(precision)).float()
-    y = core @ wo.T  # attention orientation
+    y = gated @ wo.T  # attention orientation
+    # one rounding of each gated value (half an ulp, relative) bounds the difference
+    rel = 2.0 ** -8 if precision == "bf16" else 2.0 ** -11
+    bound = 1.5 * rel * (gated.abs() @ wo.abs().T) + 1e-5
     if not starting:
-        y = y.transpose(1, 2)
+        y, bound = y.transpose(1, 2), bound.transpose(1, 2)
     if residual:
         y = y + ctx["z"]
-    torch.testing.assert_close(out.cpu(), y, rtol=1e-4, atol=1e-4)
+        bound = bound + 1e-6 * ctx["z"].abs()
+    err = (out.cpu() - y).abs()
+    assert torch.isfinite(out.cpu()).all()
+    assert (err <= bound).all(), float((err - bound).max())
