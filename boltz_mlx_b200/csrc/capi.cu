@@ -28,6 +28,21 @@ int* device_status_ptr() {
   return cache[dev];
 }
 
+// Multiprocessor count of the current device, resolved once per device.
+int device_sm_count() {
+  static int cache[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 1;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 }  // namespace triattn
 
 using namespace triattn;
@@ -110,6 +125,7 @@ LayerArgs make_args(int B, int N, int starting, int row_begin, int row_end, floa
   a.ws = static_cast<unsigned char*>(ws);
   a.wl = Workspace::make(B, N, row_end - row_begin, dtype);
   a.status = device_status_ptr();
+  a.num_sms = device_sm_count();
   return a;
 }
 

@@ -38,35 +38,41 @@ __device__ __forceinline__ float ex2(float x) {
 }  // namespace
 
 // =================================================================================================
-// LN + q|k|v|g projection (+ tri bias).  CTA = 128 pairs (a, c0..c0+127) of one attention row,
-// 256 threads (8 warps).  TMEM: 512 columns = the full 128 x 512 fp32 accumulator.
+// LN + q|k|v|g projection (+ tri bias).  Persistent: one CTA per SM (512 threads) loads the 128 KB
+// weight image once and walks the 128-pair tiles (a, c0..c0+127) tile = blockIdx.x, + gridDim.x, ...
+// Per tile: LayerNorm (warp w: pairs 8w..8w+7, lane: channels 4 lane..+3) -> operand image in shared
+// memory + tri-bias rows; the z rows of the next tile are loaded into registers right after the
+// LayerNorm, so their HBM latency overlaps the MMA and the epilogue.  MMA: D[128 x 512] = xn * W^T
+// in two N=256 halves (q|k, v|g) with separate commits, so the q|k epilogue starts while v|g runs.
+// Epilogue: warp w reads TMEM lanes 32 (w % 4).. and writes output type w / 4 (q, k, v, g).
+// TMEM: 512 columns = the full 128 x 512 fp32 accumulator of one tile.
 // =================================================================================================
+constexpr int LP_THREADS = 512;
 constexpr int LP_W_BYTES = NPROJ * C_IN * 2;  // 131072
 constexpr int LP_A_BYTES = TILE * C_IN * 2;   // 32768
-constexpr int LP_SMEM = LP_W_BYTES + LP_A_BYTES + HEADS * TILE * 4 + 64;
+constexpr int LP_SMEM = LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + 64;
 
 template <typename T>
-__global__ void __launch_bounds__(256, 1) ln_proj_tc_kernel(LayerArgs args) {
+__global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sW = smem;
   unsigned char* sA = smem + LP_W_BYTES;
-  float* sBias = reinterpret_cast<float*>(smem + LP_W_BYTES + LP_A_BYTES);  // [4][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + LP_A_BYTES + HEADS * TILE * 4);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  float* sBias = reinterpret_cast<float*>(smem + LP_W_BYTES + LP_A_BYTES);  // [2][4][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
   uint64_t* bar_w = bars;
-  uint64_t* bar_mma = bars + 1;
+  uint64_t* bar_mma = bars + 1;  // [2]: q|k half, v|g half
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ct = blockIdx.x, c0 = ct * TILE;
-  const int al = blockIdx.y, a = args.row_begin + al;
-  const int b = blockIdx.z;
   const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT;
+  const int ntiles = NT * R * args.B;
   const float* P = reinterpret_cast<const float*>(args.packed);
   int* status = args.status;
 
   if (tid == 0) {
     mbar_init(bar_w, 1);
-    mbar_init(bar_mma, 1);
+    mbar_init(bar_mma + 0, 1);
+    mbar_init(bar_mma + 1, 1);
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(tslot, 512);
@@ -74,103 +80,120 @@ __global__ void __launch_bounds__(256, 1) ln_proj_tc_kernel(LayerArgs args) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  if (tid == 0) {
+  if (tid == 0 && (int)blockIdx.x < ntiles) {
     mbar_arrive_expect_tx(bar_w, LP_W_BYTES);
     bulk_g2s(sW, args.packed + PackedLayout::img_qkvg, LP_W_BYTES, bar_w);
   }
 
-  // ---- LayerNorm: warp w handles rows 16w..16w+15; lane owns channels 4*lane..4*lane+3 ----
   const float4 lw = reinterpret_cast<const float4*>(P + PackedLayout::ln_w / 4)[lane];
   const float4 lb = reinterpret_cast<const float4*>(P + PackedLayout::ln_b / 4)[lane];
   float4 wb[HEADS];
 #pragma unroll
   for (int hh = 0; hh < HEADS; ++hh) wb[hh] = reinterpret_cast<const float4*>(P + PackedLayout::w_b / 4 + hh * C_IN)[lane];
-  float4 xv[16];
+  // this warp's 8 z rows of a tile (zeros past N)
+  auto load_rows = [&](int tile, float4 (&xv)[8]) {
+    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+    const float* zr = args.z + b * args.zv.s_batch + (long long)(args.row_begin + al - args.zv.row0) * args.zv.s_row;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int c = c0 + warp * 16 + i;
-    xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < N) {
-      const float* x = args.z + b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row +
-                       (long long)c * args.zv.s_col;
-      xv[i] = __ldg(reinterpret_cast<const float4*>(x) + lane);
+    for (int i = 0; i < 8; ++i) {
+      const int c = ct * TILE + warp * 8 + i;
+      xv[i] = c < N ? __ldcs(reinterpret_cast<const float4*>(zr + (long long)c * args.zv.s_col) + lane)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-  }
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int r = warp * 16 + i;
-    const float4 v = xv[i];
-    const float mean = warp_sum32(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
-    const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
-    const float var = warp_sum32(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / C_IN);
-    const float rstd = 1.0f / sqrtf(var + LN_EPS);
-    const float n0 = d0 * rstd * lw.x + lb.x, n1 = d1 * rstd * lw.y + lb.y;
-    const float n2 = d2 * rstd * lw.z + lb.z, n3 = d3 * rstd * lw.w + lb.w;
-    uint2 pk;
-    pk.x = H16<T>::pack(n0, n1);
-    pk.y = H16<T>::pack(n2, n3);
-    *reinterpret_cast<uint2*>(sA + img_off(r, 4 * lane, C_IN)) = pk;
-    float tbv[HEADS];
-#pragma unroll
-    for (int hh = 0; hh < HEADS; ++hh)
-      tbv[hh] = warp_sum32(n0 * wb[hh].x + n1 * wb[hh].y + n2 * wb[hh].z + n3 * wb[hh].w);
-    if (lane == 0) {
-#pragma unroll
-      for (int hh = 0; hh < HEADS; ++hh) sBias[hh * TILE + r] = tbv[hh];
-    }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
+  };
+  float4 xv[8];
+  int tile = blockIdx.x;
+  if (tile < ntiles) load_rows(tile, xv);
 
-  // ---- tri-bias rows of attention row a: fp16, log2 domain, 128 x 128 block layout [k/8][q][8];
-  //      one 16-byte chunk = 8 consecutive keys of one head (padded keys 0) ----
-  if (tid < HEADS * (TILE / 8)) {
-    const int hh = tid / (TILE / 8), kg = tid % (TILE / 8);
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r0 = kg * 8 + 2 * i;
-      const float v0 = c0 + r0 < N ? sBias[hh * TILE + r0] * LOG2E : 0.0f;
-      const float v1 = c0 + r0 + 1 < N ? sBias[hh * TILE + r0 + 1] * LOG2E : 0.0f;
-      w[i] = H16<__half>::pack(v0, v1);
-    }
-    *reinterpret_cast<uint4*>(args.ws + args.wl.off_bias + bias16_off(a, c0 + kg * 8, b, hh, args.B, NT)) =
-        make_uint4(w[0], w[1], w[2], w[3]);
-  }
+  for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
+    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+    const int a = args.row_begin + al, c0 = ct * TILE;
+    float* sB = sBias + (it & 1) * HEADS * TILE;
 
-  // ---- MMA: D[128 x 512] = xn[128 x 128] * W_qkvg[512 x 128]^T, two N=256 halves ----
-  if (tid == 0) {
-    mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
+    // ---- LayerNorm of this warp's 8 rows -> operand image + tri-bias values ----
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = warp * 8 + i;
+      const float4 v = xv[i];
+      const float mean = warp_sum32(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
+      const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+      const float var = warp_sum32(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / C_IN);
+      const float rstd = 1.0f / sqrtf(var + LN_EPS);
+      const float n0 = d0 * rstd * lw.x + lb.x, n1 = d1 * rstd * lw.y + lb.y;
+      const float n2 = d2 * rstd * lw.z + lb.z, n3 = d3 * rstd * lw.w + lb.w;
+      uint2 pk;
+      pk.x = H16<T>::pack(n0, n1);
+      pk.y = H16<T>::pack(n2, n3);
+      *reinterpret_cast<uint2*>(sA + img_off(r, 4 * lane, C_IN)) = pk;
+      // four head sums at once: exchange halves (xor 16: heads 0,1 | 2,3; xor 8: one head each), then
+      // three more butterfly steps; lane 8 hh ends with head hh's total
+      float p[HEADS];
+#pragma unroll
+      for (int hh = 0; hh < HEADS; ++hh) p[hh] = n0 * wb[hh].x + n1 * wb[hh].y + n2 * wb[hh].z + n3 * wb[hh].w;
+      const bool up16 = lane & 16, up8 = lane & 8;
+      float k0 = up16 ? p[2] : p[0], k1 = up16 ? p[3] : p[1];
+      k0 += __shfl_xor_sync(0xffffffffu, up16 ? p[0] : p[2], 16);
+      k1 += __shfl_xor_sync(0xffffffffu, up16 ? p[1] : p[3], 16);
+      float k = up8 ? k1 : k0;
+      k += __shfl_xor_sync(0xffffffffu, up8 ? k0 : k1, 8);
+      k += __shfl_xor_sync(0xffffffffu, k, 4);
+      k += __shfl_xor_sync(0xffffffffu, k, 2);
+      k += __shfl_xor_sync(0xffffffffu, k, 1);
+      if ((lane & 7) == 0) sB[(lane >> 3) * TILE + r] = k;
+    }
+    // the next tile's rows: in flight during the MMA and the epilogue
+    if (tile + (int)gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();  // image + tri-bias values complete; previous epilogue done with TMEM
     tc_fence_after();
-    constexpr uint32_t idesc = make_idesc_f16(128, 256, H16<T>::is_bf16, 0, 0);
-#pragma unroll
-    for (int ks = 0; ks < C_IN / 16; ++ks) {
-      const uint64_t ad = smem_desc_noswizzle(smem_u32(sA) + ks * 256, 128, 16 * C_IN);
+
+    // ---- MMA: two N=256 halves, one commit each ----
+    if (tid == 0) {
+      if (it == 0) mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
+      tc_fence_after();
+      constexpr uint32_t idesc = make_idesc_f16(128, 256, H16<T>::is_bf16, 0, 0);
 #pragma unroll
       for (int nh = 0; nh < 2; ++nh) {
-        const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * C_IN);
-        umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < C_IN / 16; ++ks) {
+          const uint64_t ad = smem_desc_noswizzle(smem_u32(sA) + ks * 256, 128, 16 * C_IN);
+          const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * C_IN);
+          umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_mma + nh);
       }
     }
-    umma_commit(bar_mma);
-  }
-  __syncwarp();
-  mbar_wait(bar_mma, 0, status, DEV_TIMEOUT_MMA);
-  __syncwarp();
-  tc_fence_after();
 
-  // ---- epilogue: warp w reads lanes 32*(w%4).., column half w/4 (q|k or v|g) ----
-  const int quad = warp & 3, half = warp >> 2;
-  const int r = quad * 32 + lane, c = c0 + r;
-  const bool valid = c < N;
-#pragma unroll 1
-  for (int t = 0; t < 2; ++t) {
-    const int tt = half * 2 + t;  // 0 q, 1 k, 2 v, 3 g
+    // ---- tri-bias rows of attention row a: fp16, log2 domain, 128 x 128 block layout [k/8][q][8];
+    //      one 16-byte chunk = 8 consecutive keys of one head (padded keys 0) ----
+    if (tid < HEADS * (TILE / 8)) {
+      const int hh = tid / (TILE / 8), kg = tid % (TILE / 8);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r0 = kg * 8 + 2 * i;
+        const float v0 = c0 + r0 < N ? sB[hh * TILE + r0] * LOG2E : 0.0f;
+        const float v1 = c0 + r0 + 1 < N ? sB[hh * TILE + r0 + 1] * LOG2E : 0.0f;
+        w[i] = H16<__half>::pack(v0, v1);
+      }
+      *reinterpret_cast<uint4*>(args.ws + args.wl.off_bias + bias16_off(a, c0 + kg * 8, b, hh, args.B, NT)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+
+    // ---- epilogue: warp w reads lanes 32*(w%4).., output type w/4 (0 q, 1 k, 2 v, 3 g) ----
+    const int quad = warp & 3, tt = warp >> 2;
+    const int r = quad * 32 + lane, c = c0 + r;
+    const bool valid = c < N;
+    mbar_wait(bar_mma + (tt >> 1), it & 1, status, DEV_TIMEOUT_MMA);
+    __syncwarp();
+    tc_fence_after();
 #pragma unroll 1
     for (int hh = 0; hh < HEADS; ++hh) {
       uint32_t acc[32];
       tmem_ld32(tmem_addr(tbase, quad * 32, tt * 128 + hh * 32), acc);
       tmem_ld_wait();
+      tmem_regs_ready(acc);
       if (tt == 0 || tt == 1) {
         // q (pre-scaled by C^-1/2 log2 e: the core's S is then in log2 units) and k: K-major images
         const float sc = tt == 0 ? QSCALE_L2 : 1.0f;
@@ -217,18 +240,21 @@ __global__ void __launch_bounds__(256, 1) ln_proj_tc_kernel(LayerArgs args) {
         }
       }
     }
+    // both MMA halves read the operand image, which the next LayerNorm overwrites
+    if (tt < 2) mbar_wait(bar_mma + 1, it & 1, status, DEV_TIMEOUT_MMA);
+    tc_fence_before();
   }
-  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
 template <typename T>
 static cudaError_t ln_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
   cudaFuncSetAttribute(ln_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM);
-  const int R = a.row_end - a.row_begin;
-  dim3 grid(a.wl.NT, R, a.B);
-  ln_proj_tc_kernel<T><<<grid, 256, LP_SMEM, st>>>(a);
+  const int ntiles = a.wl.NT * (a.row_end - a.row_begin) * a.B;
+  const int grid = ntiles < a.num_sms ? ntiles : a.num_sms;
+  ln_proj_tc_kernel<T><<<grid, LP_THREADS, LP_SMEM, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -746,21 +772,24 @@ __global__ void __launch_bounds__(128) out_proj_tc_kernel(LayerArgs args) {
   const bool valid = c < N;
   const long long ooff = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row + (long long)c * args.ov.s_col;
   const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row + (long long)c * args.zv.s_col;
+  // 32 output channels per step; the residual values of a step are all loaded before any store
+  // (out may alias z, so the compiler would otherwise serialise every load behind the previous store)
 #pragma unroll 1
   for (int cch = 0; cch < 4; ++cch) {
+    float4 zz[8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d)
+      zz[d] = (valid && args.add_residual) ? __ldcs(reinterpret_cast<const float4*>(args.z + zoff + cch * 32) + d)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
     uint32_t acc[32];
     tmem_ld32(tmem_addr(tbase, warp * 32, cch * 32), acc);
     tmem_ld_wait();
     if (valid) {
 #pragma unroll
-      for (int d = 0; d < 32; d += 4) {
-        float4 y = make_float4(__uint_as_float(acc[d]), __uint_as_float(acc[d + 1]), __uint_as_float(acc[d + 2]),
-                               __uint_as_float(acc[d + 3]));
-        if (args.add_residual) {
-          const float4 zz = *reinterpret_cast<const float4*>(args.z + zoff + cch * 32 + d);
-          y.x += zz.x; y.y += zz.y; y.z += zz.z; y.w += zz.w;
-        }
-        *reinterpret_cast<float4*>(args.out + ooff + cch * 32 + d) = y;
+      for (int d = 0; d < 8; ++d) {
+        const float4 y = make_float4(__uint_as_float(acc[4 * d]) + zz[d].x, __uint_as_float(acc[4 * d + 1]) + zz[d].y,
+                                     __uint_as_float(acc[4 * d + 2]) + zz[d].z, __uint_as_float(acc[4 * d + 3]) + zz[d].w);
+        __stcs(reinterpret_cast<float4*>(args.out + ooff + cch * 32) + d, y);
       }
     }
   }

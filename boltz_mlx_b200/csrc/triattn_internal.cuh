@@ -122,6 +122,7 @@ struct LayerArgs {
   unsigned char* ws;
   Workspace wl;
   int* status;                 // device status word
+  int num_sms;                 // multiprocessors of the current device (persistent grids)
 };
 
 // launchers (return cudaGetLastError())
