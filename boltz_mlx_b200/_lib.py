@@ -110,7 +110,8 @@ def stream_handle(device: torch.device) -> int:
 
 
 def device_status(clear: bool = True) -> int:
-    """The device status word (0 = ok; 101..104 = a bounded wait ran out / bad index).  Synchronises."""
+    """The device status word (0 = ok; 101..103 = a bounded wait ran out, 104 bad index, 105 unaligned
+    shared memory).  Synchronises."""
     v = ctypes.c_int(0)
     check(lib().triattn_device_status(ctypes.byref(v), int(clear)))
     return v.value

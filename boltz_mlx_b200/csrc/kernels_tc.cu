@@ -50,7 +50,7 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr int LP_THREADS = 512;
 constexpr int LP_W_BYTES = NPROJ * C_IN * 2;  // 131072
 constexpr int LP_A_BYTES = TILE * C_IN * 2;   // 32768
-constexpr int LP_SMEM = LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + 64;
+constexpr int LP_SMEM = LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4 + 64;
 
 template <typename T>
 __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs args) {
@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   unsigned char* sW = smem;
   unsigned char* sA = smem + LP_W_BYTES;
   float* sBias = reinterpret_cast<float*>(smem + LP_W_BYTES + LP_A_BYTES);  // [2][4][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4);
+  float* sGb = reinterpret_cast<float*>(smem + LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4);  // g bias [128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
   uint64_t* bar_w = bars;
   uint64_t* bar_mma = bars + 1;  // [2]: q|k half, v|g half
@@ -69,12 +70,18 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   const float* P = reinterpret_cast<const float*>(args.packed);
   int* status = args.status;
 
+  // the swizzled operand image needs a 1024-byte aligned base (uniform over the CTA)
+  if ((smem_u32(sA) & 1023u) != 0) {
+    if (tid == 0) atomicCAS(status, 0, (int)DEV_BAD_ALIGN);
+    return;
+  }
   if (tid == 0) {
     mbar_init(bar_w, 1);
     mbar_init(bar_mma + 0, 1);
     mbar_init(bar_mma + 1, 1);
     fence_mbar_init();
   }
+  if (tid < C_IN) sGb[tid] = P[PackedLayout::g_b / 4 + tid];
   if (warp == 0) tmem_alloc(tslot, 512);
   tc_fence_before();
   __syncthreads();
@@ -118,13 +125,14 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
       const float mean = warp_sum32(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
       const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
       const float var = warp_sum32(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / C_IN);
-      const float rstd = 1.0f / sqrtf(var + LN_EPS);
+      const float rstd = rsqrtf(var + LN_EPS);
       const float n0 = d0 * rstd * lw.x + lb.x, n1 = d1 * rstd * lw.y + lb.y;
       const float n2 = d2 * rstd * lw.z + lb.z, n3 = d3 * rstd * lw.w + lb.w;
       uint2 pk;
       pk.x = H16<T>::pack(n0, n1);
       pk.y = H16<T>::pack(n2, n3);
-      *reinterpret_cast<uint2*>(sA + img_off(r, 4 * lane, C_IN)) = pk;
+      // swizzled image: one row's 256 bytes are two 128-byte runs (no bank conflicts)
+      *reinterpret_cast<uint2*>(sA + sw128_off(r, 4 * lane, LP_A_BYTES / 2)) = pk;
       // four head sums at once: exchange halves (xor 16: heads 0,1 | 2,3; xor 8: one head each), then
       // three more butterfly steps; lane 8 hh ends with head hh's total
       float p[HEADS];
@@ -157,7 +165,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
       for (int nh = 0; nh < 2; ++nh) {
 #pragma unroll
         for (int ks = 0; ks < C_IN / 16; ++ks) {
-          const uint64_t ad = smem_desc_noswizzle(smem_u32(sA) + ks * 256, 128, 16 * C_IN);
+          const uint64_t ad = smem_desc_sw128(smem_u32(sA) + (ks / 4) * (LP_A_BYTES / 2) + (ks % 4) * 32);
           const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * C_IN);
           umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
         }
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
           *reinterpret_cast<uint4*>(img + vimg_off(r, d)) = pk;
         }
       } else if (valid) {
-        const float* gb = P + PackedLayout::g_b / 4 + hh * C_HEAD;
+        const float* gb = sGb + hh * C_HEAD;
         T* g = reinterpret_cast<T*>(args.ws + args.wl.off_g) + (((size_t)b * R + al) * N + c) * C_IN + hh * C_HEAD;
 #pragma unroll
         for (int d = 0; d < C_HEAD; d += 8) {
@@ -695,17 +703,21 @@ cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 
 // =================================================================================================
 // Output projection (+ residual).  CTA = 128 pairs; y[128 x 128] = (core o sigmoid(g))[128 x 128] * W_o^T.
+// 256 threads: thread (part, row) gates channels 64 part .. + 64 of one query row, then reads TMEM
+// lanes of that row's quadrant for output channels 64 part .. + 64; every global load of a thread
+// is issued before it waits (g before the bulk copy lands, the residual before the MMA ends).
 // =================================================================================================
+constexpr int OP_THREADS = 256;
 constexpr int OP_SMEM = 65536 + 64;
 
 template <typename T>
-__global__ void __launch_bounds__(128) out_proj_tc_kernel(LayerArgs args) {
+__global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
   unsigned char* sW = smem + 32768;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 65536);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ct = blockIdx.x, al = blockIdx.y, a = args.row_begin + al, b = blockIdx.z;
   const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT;
   int* status = args.status;
@@ -724,31 +736,30 @@ __global__ void __launch_bounds__(128) out_proj_tc_kernel(LayerArgs args) {
     bulk_g2s(sA, args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + ct) * 32768, 32768, bars + 0);
     bulk_g2s(sW, args.packed + PackedLayout::img_o, 32768, bars + 0);
   }
-  // gate: the fp16 core image row of query ct*128 + tid times sigmoid(g) of the same (b, row, query),
-  // rounded once to T, in place (the MMA then reads a T image)
+  // gate: the fp16 core image row times sigmoid(g) of the same (b, row, query), rounded once to T,
+  // in place (the MMA then reads a T image)
   {
-    const int q = min(ct * TILE + tid, N - 1);
-    const uint4* g = reinterpret_cast<const uint4*>(args.ws + args.wl.off_g + (((size_t)b * R + al) * N + q) * C_IN * 2);
+    const int row = tid & 127, part = tid >> 7;
+    const int q = min(ct * TILE + row, N - 1);
+    const uint4* g = reinterpret_cast<const uint4*>(args.ws + args.wl.off_g + (((size_t)b * R + al) * N + q) * C_IN * 2) +
+                     8 * part;
+    uint4 gv[8];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint4 gv[8];
+    for (int i = 0; i < 8; ++i) gv[i] = __ldcs(g + i);
+    mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) gv[i] = __ldcs(g + 8 * half + i);
-      if (half == 0) mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
+    for (int i = 0; i < 8; ++i) {
+      uint4* cp = reinterpret_cast<uint4*>(sA + img_off(row, 8 * (8 * part + i), HC));
+      const uint4 cv = *cp;
+      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
+      uint32_t ow[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint4* cp = reinterpret_cast<uint4*>(sA + img_off(tid, 8 * (8 * half + i), HC));
-        const uint4 cv = *cp;
-        const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
-        uint32_t ow[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 c2 = H16<__half>::unpack(cw[e]);
-          const float2 g2 = H16<T>::unpack(gw[e]);
-          ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
-        }
-        *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      for (int e = 0; e < 4; ++e) {
+        const float2 c2 = H16<__half>::unpack(cw[e]);
+        const float2 g2 = H16<T>::unpack(gw[e]);
+        ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
       }
+      *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
   }
   fence_proxy_async_smem();
@@ -764,32 +775,38 @@ __global__ void __launch_bounds__(128) out_proj_tc_kernel(LayerArgs args) {
     }
     umma_commit(bars + 1);
   }
+  // epilogue: warp w reads TMEM lanes 32 (w % 4).. (its rows), output channels 64 (w / 4) .. + 64
+  const int quad = warp & 3, part = warp >> 2;
+  const int c = ct * TILE + quad * 32 + lane;
+  const bool valid = c < N;
+  const long long ooff = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row + (long long)c * args.ov.s_col +
+                         64 * part;
+  const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row + (long long)c * args.zv.s_col +
+                         64 * part;
+  // all 16 residual float4 of this thread in flight before the MMA wait (out may alias z, so every
+  // load is issued before the first store)
+  float4 zz[16];
+#pragma unroll
+  for (int d = 0; d < 16; ++d)
+    zz[d] = (valid && args.add_residual) ? __ldcs(reinterpret_cast<const float4*>(args.z + zoff) + d)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
   __syncwarp();
   mbar_wait(bars + 1, 0, status, DEV_TIMEOUT_MMA);
   __syncwarp();
   tc_fence_after();
-  const int c = ct * TILE + tid;
-  const bool valid = c < N;
-  const long long ooff = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row + (long long)c * args.ov.s_col;
-  const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row + (long long)c * args.zv.s_col;
-  // 32 output channels per step; the residual values of a step are all loaded before any store
-  // (out may alias z, so the compiler would otherwise serialise every load behind the previous store)
-#pragma unroll 1
-  for (int cch = 0; cch < 4; ++cch) {
-    float4 zz[8];
 #pragma unroll
-    for (int d = 0; d < 8; ++d)
-      zz[d] = (valid && args.add_residual) ? __ldcs(reinterpret_cast<const float4*>(args.z + zoff + cch * 32) + d)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int h2 = 0; h2 < 2; ++h2) {
     uint32_t acc[32];
-    tmem_ld32(tmem_addr(tbase, warp * 32, cch * 32), acc);
+    tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
     tmem_ld_wait();
+    tmem_regs_ready(acc);
     if (valid) {
 #pragma unroll
       for (int d = 0; d < 8; ++d) {
-        const float4 y = make_float4(__uint_as_float(acc[4 * d]) + zz[d].x, __uint_as_float(acc[4 * d + 1]) + zz[d].y,
-                                     __uint_as_float(acc[4 * d + 2]) + zz[d].z, __uint_as_float(acc[4 * d + 3]) + zz[d].w);
-        __stcs(reinterpret_cast<float4*>(args.out + ooff + cch * 32) + d, y);
+        const float4 zd = zz[8 * h2 + d];
+        const float4 y = make_float4(__uint_as_float(acc[4 * d]) + zd.x, __uint_as_float(acc[4 * d + 1]) + zd.y,
+                                     __uint_as_float(acc[4 * d + 2]) + zd.z, __uint_as_float(acc[4 * d + 3]) + zd.w);
+        __stcs(reinterpret_cast<float4*>(args.out + ooff) + 8 * h2 + d, y);
       }
     }
   }
@@ -803,7 +820,7 @@ static cudaError_t out_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
   cudaFuncSetAttribute(out_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
   const int R = a.row_end - a.row_begin;
   dim3 grid(a.wl.NT, R, a.B);
-  out_proj_tc_kernel<T><<<grid, 128, OP_SMEM, st>>>(a);
+  out_proj_tc_kernel<T><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -23,6 +23,7 @@ enum DeviceError : int {
   DEV_TIMEOUT_MMA = 102,
   DEV_TIMEOUT_SYNC = 103,
   DEV_BAD_INDEX = 104,
+  DEV_BAD_ALIGN = 105,  // shared-memory base not aligned as a swizzled operand needs
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -247,6 +248,26 @@ __device__ __forceinline__ uint64_t smem_desc_noswizzle(uint32_t smem_addr, uint
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
   return d;
+}
+
+// K-major operand in the 128-byte swizzled layout: 64 16-bit K values (128 B) per row, 8-row atoms
+// of 1024 B (SBO), the 16-byte chunk index XORed with row % 8:
+//       byte(row, k) = (row / 8) * 1024 + (row % 8) * 128 + (((k % 64) / 8) ^ (row % 8)) * 16 + (k % 8) * 2
+//                      + (k / 64) * kblock_bytes
+// The atom base must be 1024-byte aligned; a K step of 16 inside an atom advances the start by 32 B.
+// Bits as above with layout (bits [61,64)) = 2 (SWIZZLE_128B); LBO unused.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>((1024u >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+__host__ __device__ __forceinline__ uint32_t sw128_off(int row, int k, int kblock_bytes) {
+  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2 +
+                    (k >> 6) * kblock_bytes);
 }
 
 // Instruction descriptor for kind::f16 with fp32 accumulate.

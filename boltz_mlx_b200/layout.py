@@ -37,6 +37,15 @@ def img_offsets(rows: int, kdim: int) -> np.ndarray:
     return (r % 8) * 16 + (r // 8) * (16 * kdim) + (k % 8) * 2 + (k // 8) * 128
 
 
+def sw128_offsets(rows: int, kdim: int) -> np.ndarray:
+    """Byte offset of (row, k) in a 128-byte swizzled K-major image (the LayerNorm operand of the
+    projection MMA): 64-element K blocks of rows * 128 bytes, 8-row atoms of 1024 bytes, the 16-byte
+    chunk index XORed with row % 8.  Shape [rows, kdim]."""
+    r = np.arange(rows)[:, None]
+    k = np.arange(kdim)[None, :]
+    return (r // 8) * 1024 + (r % 8) * 128 + ((((k % 64) // 8) ^ (r % 8)) * 16) + (k % 8) * 2 + (k // 64) * rows * 128
+
+
 @dataclass
 class Workspace:
     B: int

@@ -70,7 +70,9 @@ TRIATTN_API const char* triattn_version(void);
 /* Human-readable text of the last host-side error on the calling thread (static storage). */
 TRIATTN_API const char* triattn_last_error_string(void);
 
-/* Read the device status word of the current device (0 = ok); clear it when `clear` != 0.
+/* Read the device status word of the current device (0 = ok; 101 a bulk copy, 102 an MMA, 103 a
+ * barrier wait ran out; 104 an index check failed; 105 a shared-memory base was not aligned as a
+ * swizzled operand needs); clear it when `clear` != 0.
  * Synchronises the device.  Returns TRIATTN_OK and writes the word to *status. */
 TRIATTN_API int triattn_device_status(int* status, int clear);
 

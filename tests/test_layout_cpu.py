@@ -5,7 +5,7 @@ descriptors of the consumers read, for every MMA the kernels issue."""
 import numpy as np
 import pytest
 
-from boltz_mlx_b200.layout import TILE, Workspace, img_offsets
+from boltz_mlx_b200.layout import TILE, Workspace, img_offsets, sw128_offsets
 
 
 def kmajor_desc_addr(start, lbo, sbo, rows, kdim):
@@ -20,6 +20,16 @@ def mnmajor_desc_addr(start, lbo, sbo, mn, kdim):
     m = np.arange(mn)[:, None]
     k = np.arange(kdim)[None, :]
     return start + (k % 8) * 16 + (k // 8) * lbo + (m % 8) * 2 + (m // 8) * sbo
+
+
+def sw128_desc_addr(start, rows, kdim):
+    """Bytes read by a 128-byte-swizzle K-major descriptor (SBO 1024) for rows x kdim 16-bit values:
+    the unswizzled address start + (r // 8) * 1024 + (r % 8) * 128 + 2 k, then the hardware XORs
+    address bits [4,7) with bits [7,10) (the start must keep the atom 1024-byte aligned)."""
+    r = np.arange(rows)[:, None]
+    k = np.arange(kdim)[None, :]
+    a = start + (r // 8) * 1024 + (r % 8) * 128 + 2 * k
+    return a ^ (((a >> 7) & 7) << 4)
 
 
 @pytest.mark.parametrize("kdim", [32, 128])
@@ -56,12 +66,24 @@ def test_pv_mma_reads_v_image_as_mn_major():
 def test_projection_mma_w_halves(n_half):
     """D[128 x 512] in two N=256 MMAs: B half h starts at +65536 B, K steps of 16 at +256 B."""
     woff = img_offsets(512, 128)
-    aoff = img_offsets(TILE, 128)
+    aoff = sw128_offsets(TILE, 128)
     for ks in range(8):
-        a = kmajor_desc_addr(ks * 256, 128, 2048, TILE, 16)
+        # A: swizzled LayerNorm image, K block ks // 4 at +16 KB, K step ks % 4 at +32 B inside an atom
+        a = sw128_desc_addr((ks // 4) * TILE * 128 + (ks % 4) * 32, TILE, 16)
         assert np.array_equal(a, aoff[:, ks * 16:(ks + 1) * 16])
         b = kmajor_desc_addr(n_half * 65536 + ks * 256, 128, 2048, 256, 16)
         assert np.array_equal(b, woff[n_half * 256:(n_half + 1) * 256, ks * 16:(ks + 1) * 16])
+
+
+def test_sw128_image_rows_are_two_contiguous_runs():
+    """The swizzled image is a dense bijection, and one row's 128 channels are two 128-byte runs
+    (a warp storing one row touches each shared-memory bank once per run)."""
+    off = sw128_offsets(TILE, 128)
+    assert len(np.unique(off)) == TILE * 128 and off.min() == 0 and off.max() == TILE * 256 - 2
+    for r in range(TILE):
+        for kb in range(2):
+            run = np.sort(off[r, 64 * kb:64 * kb + 64])
+            assert run[0] % 128 == 0 and np.array_equal(np.diff(run), np.full(63, 2))
 
 
 def test_p_tmem_columns_pack_key_pairs():
