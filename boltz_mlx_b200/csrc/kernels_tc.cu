@@ -273,7 +273,7 @@ cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 // =================================================================================================
 // Mask bias + key-tile classes (16-bit path).  One CTA per (attention row, batch), 128 threads.
 //   mb[b][row][k] = log2(e) * inf * (mask - 1)  (k < N),  -1e30 for padded keys
-//   ts[b][row][kt] = 0 every key of the tile valid, 1 every key masked and the row has a valid key
+//   ts[b][row][kt] (row stride NTs) = 0 every key of the tile valid, 1 every key masked and the row has a valid key
 //   elsewhere (the tile contributes exactly 0 and is skipped), 2 otherwise (mask bias applied; a
 //   row with no valid key at all keeps every tile, which makes it attend uniformly, as in fp32).
 // =================================================================================================
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(128) mask_prep_tc_kernel(LayerArgs args) {
     }
   }
   __syncthreads();
-  uint8_t* ts = args.ws + args.wl.off_ts + ((size_t)b * R + al) * NT;
+  uint8_t* ts = args.ws + args.wl.off_ts + ((size_t)b * R + al) * args.wl.NTs;
   for (int kt = tid; kt < NT; kt += blockDim.x) ts[kt] = any_valid ? cls[kt] : 2;
 }
 
@@ -315,13 +315,17 @@ cudaError_t launch_mask_prep_tc(const LayerArgs& a, cudaStream_t st) {
 }
 
 // =================================================================================================
-// Flash core.  CTA = (batch b, head h, 128-query tile qt, group of RG attention rows); the tri-bias
-// tile of (h, qt, kt) is loaded once per key tile and shared by the RG rows.
-//   16 warps = four softmax warpgroups; warpgroup j owns row j of the group (TMEM lanes = queries).
+// Flash core, persistent.  A work item = (batch b, head h, 128-query tile qt, group of RG attention
+// rows); items are numbered with qt fastest (CTAs running at the same time read the same rows' K/V
+// tiles, which stay in L2) and CTA c takes items c, c + gridDim.x, ...  The tri-bias tile of
+// (h, qt, kt) is loaded once per key tile and shared by the RG rows of the item.
+//   16 warps = four softmax warpgroups; warpgroup j owns row j of the item (TMEM lanes = queries).
 //   Each row's leader thread issues that row's work itself: the bulk copies of its Q, K and V tiles
-//   (one slot each, refilled as soon as the MMA that read the slot has completed) and its MMAs
-//   (S = Q K^T, then O = P V).  The tri-bias stages (double-buffered) are refilled by whichever warp
-//   is the last of the 16 to finish reading a stage (an arrival counter in shared memory).
+//   (one slot each, refilled as soon as the MMA that read the slot has completed; after the row's
+//   last tile of an item they are refilled with the first active tile of the row's next item) and
+//   its MMAs (S = Q K^T, then O = P V).  The tri-bias stages form one ring over the CTA's whole
+//   sequence of (item, key tile) steps; a stage is refilled by whichever warp is the last of the 16
+//   to finish reading it (an arrival counter in shared memory).
 // TMEM (512 columns): row j owns columns [128 j, 128 j + 128): S (fp32, log2 units) -> x (after the
 // biases) -> P (fp16 pairs in columns 0..63) and the P.V partial (columns 64..111: 32 channels + the
 // row sum from V's ones column).  O is accumulated in registers with a lazy rescale.
@@ -336,15 +340,45 @@ constexpr int CG_SMB = CG_SB + CG_NB * 32768;      // NB stages x RG mask-bias s
 constexpr int CG_SK = CG_SMB + CG_NB * CG_RG * 512;  // one K slot per row, 8 KB
 constexpr int CG_SV = CG_SK + CG_RG * 8192;        // one V slot per row, 12 KB (8 KB V + 4 KB ones/zeros)
 constexpr int CG_BAR = CG_SV + CG_RG * 12288;
-constexpr int CG_CLS = CG_BAR + 512;               // RG x 128 key-tile classes
-constexpr int CG_CNT = CG_CLS + CG_RG * TILE;      // NB tri-bias stage arrival counters
-constexpr int CG_SMEM = CG_CNT + 16;
+constexpr int CG_CLS = CG_BAR + 512;               // 2 (item parity) x RG x 128 key-tile classes
+constexpr int CG_CNT = CG_CLS + 2 * CG_RG * TILE;  // NB tri-bias stage arrival counters
+constexpr int CG_RS = CG_CNT + 16;                 // RG row states (32 B each)
+constexpr int CG_II = CG_RS + CG_RG * 32;          // 3 item-info slots (32 B each)
+constexpr int CG_SMEM = CG_II + 3 * 32;
 static_assert(CG_SMEM <= 232448, "core shared memory");
 
 // barrier slots
 constexpr int B_BF = 0, B_QF = CG_NB, B_KF = B_QF + CG_RG, B_VF = B_KF + CG_RG, B_SF = B_VF + CG_RG,
               B_OF = B_SF + CG_RG, B_COUNT = B_OF + CG_RG;
 static_assert(B_COUNT * 8 + 16 <= 512, "barrier area");
+
+// Per-row state kept by the row's leader: K/V/Q tile indices (global tile = base + kt) of the
+// current and the next item, the next item's query tile and its first active key tile.
+struct CoreRowState {
+  unsigned long long cur, nxt;
+  int nxt_qt, nxt_first;
+};
+// Per-item bias addressing: byte offsets of the tri-bias block (h, qt) and of the mask-bias row of
+// the group's first row; rows of the group inside the range (0 = no such item).
+struct CoreItemInfo {
+  unsigned long long bias_off, mb_off;
+  int nrow, pad;
+};
+
+// Work item -> (b, h, qt, first row of the group).
+struct CoreItem {
+  int b, h, qt, g0;
+};
+__device__ __forceinline__ CoreItem core_item(int item, int NT, int G) {
+  CoreItem it;
+  it.qt = item % NT;
+  const int rest = item / NT;
+  it.g0 = (rest % G) * CG_RG;
+  const int bh = rest / G;
+  it.b = bh / HEADS;
+  it.h = bh % HEADS;
+  return it;
+}
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
@@ -418,16 +452,39 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + CG_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + CG_BAR + B_COUNT * 8);
-  uint8_t* scls = smem + CG_CLS;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qt = blockIdx.x;
-  const int g0 = blockIdx.y * CG_RG;  // first local row of the group
-  const int b = blockIdx.z / HEADS, h = blockIdx.z % HEADS;
-  const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT, Np = args.wl.Np;
-  int* status = args.status;
-
-  // ---- set-up: barriers, V-slot tails, key-tile classes, TMEM ----
+  uint8_t* scls = smem + CG_CLS;  // [item parity][row][kt]
   int* bias_cnt = reinterpret_cast<int*>(smem + CG_CNT);
+  CoreItemInfo* iinfo = reinterpret_cast<CoreItemInfo*>(smem + CG_II);  // [item ordinal % 3]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT, Np = args.wl.Np, NTs = args.wl.NTs;
+  const int G = (R + CG_RG - 1) / CG_RG;
+  const int n_items = NT * G * args.B * HEADS;
+  int* status = args.status;
+  const unsigned char* ts_all = args.ws + args.wl.off_ts;
+  // key-tile classes kt = 4 w4 .. 4 w4 + 3 of row g0 + jj of an item, one byte each: 0 all valid,
+  // 1 skip, 2 mixed; 3 = no such tile, row or item
+  auto class_word = [&](int item, int jj, int w4) -> uint32_t {
+    if (item >= n_items || 4 * w4 >= NTs) return 0x03030303u;
+    const CoreItem ci = core_item(item, NT, G);
+    if (ci.g0 + jj >= R) return 0x03030303u;
+    uint32_t w = *reinterpret_cast<const uint32_t*>(ts_all + ((size_t)ci.b * R + ci.g0 + jj) * NTs + 4 * w4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (4 * w4 + i >= NT) w = (w & ~(0xFFu << (8 * i))) | (3u << (8 * i));
+    return w;
+  };
+  auto item_info = [&](int item) {
+    CoreItemInfo f{};
+    if (item < n_items) {
+      const CoreItem ci = core_item(item, NT, G);
+      f.bias_off = args.wl.off_bias + (((unsigned long long)ci.qt * args.B + ci.b) * HEADS + ci.h) * NT * 32768ull;
+      f.mb_off = args.wl.off_mb + ((unsigned long long)ci.b * R + ci.g0) * Np * 4ull;
+      f.nrow = min(CG_RG, R - ci.g0);
+    }
+    return f;
+  };
+
+  // ---- set-up (once per CTA): barriers, V-slot tails, classes of the first item, TMEM ----
   if (tid == 0) {
     for (int i = 0; i < CG_NB; ++i) mbar_init(bar + B_BF + i, 1);
     for (int j = 0; j < CG_RG; ++j) {
@@ -438,6 +495,8 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
       mbar_init(bar + B_OF + j, 1);
     }
     for (int i = 0; i < CG_NB; ++i) bias_cnt[i] = 0;
+    iinfo[0] = item_info(blockIdx.x);
+    iinfo[1] = item_info(blockIdx.x + gridDim.x);
     fence_mbar_init();
   }
   // V slot tail: channel group 4 = (1, 0, ..., 0) per key (the ones column that yields the row
@@ -447,114 +506,160 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
     uint32_t* tail = reinterpret_cast<uint32_t*>(smem + CG_SV + stg * 12288 + 8192);
     tail[w] = (w < 512 && (w & 3) == 0) ? 0x00003C00u : 0u;  // fp16 1.0 in the low half of each key's first word
   }
-  // key-tile classes (0 all valid, 1 skip, 2 mixed; 3 = row outside the range)
-  for (int i = tid; i < CG_RG * TILE; i += CG_THREADS) {
-    const int j = i / TILE, kt = i % TILE;
-    scls[i] = (g0 + j < R && kt < NT) ? args.ws[args.wl.off_ts + ((size_t)b * R + g0 + j) * NT + kt] : 3;
-  }
+  if (tid < CG_RG * 32)
+    reinterpret_cast<uint32_t*>(scls)[tid] = class_word(blockIdx.x, tid / 32, tid % 32);
   fence_proxy_async_smem();
   if (warp == 0) tmem_alloc(tslot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  const size_t head0 = ((size_t)b * R) * HEADS + h;  // + row * HEADS -> (b, row, h)
-  int nrow = 0;
-#pragma unroll
-  for (int jj = 0; jj < CG_RG; ++jj) nrow += (g0 + jj < R);
-  const unsigned char* bias_blk = args.ws + args.wl.off_bias + (((size_t)qt * args.B + b) * HEADS + h) * NT * 32768;
-  const float* mb_all = reinterpret_cast<const float*>(args.ws + args.wl.off_mb);
-  // tri-bias tile kt (+ the mask-bias slices of the group's rows) -> stage kt % NB
-  auto load_bias = [&](int kt) {
-    const int bs = kt % CG_NB;
-    mbar_arrive_expect_tx(bar + B_BF + bs, 32768 + nrow * 512);
-    bulk_g2s(smem + CG_SB + bs * 32768, bias_blk + (size_t)kt * 32768, 32768, bar + B_BF + bs);
-    for (int jj = 0; jj < CG_RG; ++jj)
-      if (g0 + jj < R)
-        bulk_g2s(smem + CG_SMB + (bs * CG_RG + jj) * 512, mb_all + ((size_t)b * R + g0 + jj) * Np + kt * TILE, 512,
-                 bar + B_BF + bs);
+  // tri-bias tile kt of item ordinal i (+ the mask-bias slices of the item's rows) -> stage s % NB,
+  // s = i * NT + kt; item infos of ordinals ii and ii + 1 are in their slots while item ii runs
+  auto load_bias = [&](int i, int kt, int ii_now) {
+    const int s = i * NT + kt;
+    const CoreItemInfo f = (i <= ii_now + 1) ? iinfo[i % 3] : item_info(blockIdx.x + i * gridDim.x);
+    if (f.nrow == 0) return;
+    const int bs = s % CG_NB;
+    mbar_arrive_expect_tx(bar + B_BF + bs, 32768 + f.nrow * 512);
+    bulk_g2s(smem + CG_SB + bs * 32768, args.ws + f.bias_off + (size_t)kt * 32768, 32768, bar + B_BF + bs);
+    for (int jj = 0; jj < f.nrow; ++jj)
+      bulk_g2s(smem + CG_SMB + (bs * CG_RG + jj) * 512, args.ws + f.mb_off + ((size_t)jj * Np + kt * TILE) * 4, 512,
+               bar + B_BF + bs);
   };
   if (tid == 0)
-    for (int kt = 0; kt < CG_NB && kt < NT; ++kt) load_bias(kt);
+    for (int s = 0; s < CG_NB; ++s) load_bias(s / NT, s % NT, 0);
 
-  {
-    // ================================ softmax warpgroups ================================
-    const int j = warp >> 2, quad = warp & 3;  // row of the group, TMEM lane quadrant
-    const int t = quad * 32 + lane;            // query within the tile = TMEM lane
-    const bool leader = (quad == 0 && lane == 0);
-    const uint32_t buf = tbase + ((uint32_t)(quad * 32) << 16) + j * 128;
-    const uint32_t buf0 = tbase + j * 128;  // lane 0 of the row's columns (MMA operands)
-    constexpr uint32_t idS = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
-    constexpr uint32_t idPV = make_idesc_f16(128, 48, 0, 0, 1);  // fp16 P (TMEM) x fp16 V (MN-major), N = 32 + 16
-    float o[C_HEAD], l = 0.f, m = 0.f;
-    bool started = false;
-    int n = 0;  // tiles processed by this row
-#pragma unroll
-    for (int d = 0; d < C_HEAD; ++d) o[d] = 0.f;
-    const bool row_ok = g0 + j < R;
-    const size_t tile0 = (head0 + (size_t)(g0 + j) * HEADS) * NT;
-    auto next_active = [&](int kt) {
-      while (kt < NT && scls[j * TILE + kt] != 0 && scls[j * TILE + kt] != 2) ++kt;
-      return kt;
-    };
-    if (leader && row_ok) {
-      mbar_arrive_expect_tx(bar + B_QF + j, 8192);
-      bulk_g2s(smem + CG_SQ + j * 8192, args.ws + args.wl.off_q + (tile0 + qt) * 8192, 8192, bar + B_QF + j);
-      const int k0 = next_active(0);
-      if (k0 < NT) {
-        mbar_arrive_expect_tx(bar + B_KF + j, 8192);
-        bulk_g2s(smem + CG_SK + j * 8192, args.ws + args.wl.off_k + (tile0 + k0) * 8192, 8192, bar + B_KF + j);
-        mbar_arrive_expect_tx(bar + B_VF + j, 8192);
-        bulk_g2s(smem + CG_SV + j * 12288, args.ws + args.wl.off_v + (tile0 + k0) * 8192, 8192, bar + B_VF + j);
+  // ================================ softmax warpgroups ================================
+  const int j = warp >> 2, quad = warp & 3;  // row of the item, TMEM lane quadrant
+  const int t = quad * 32 + lane;            // query within the tile = TMEM lane
+  const bool leader = (quad == 0 && lane == 0);
+  const uint32_t buf = tbase + ((uint32_t)(quad * 32) << 16) + j * 128;
+  const uint32_t buf0 = tbase + j * 128;  // lane 0 of the row's columns (MMA operands)
+  constexpr uint32_t idS = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
+  constexpr uint32_t idPV = make_idesc_f16(128, 48, 0, 0, 1);  // fp16 P (TMEM) x fp16 V (MN-major), N = 32 + 16
+  CoreRowState* rs = reinterpret_cast<CoreRowState*>(smem + CG_RS) + j;
+  // first active key tile >= kt of row j in the item whose classes are in slot cs
+  auto next_active = [&](int cs, int kt) {
+    const uint8_t* c = scls + (cs * CG_RG + j) * TILE;
+    while (kt < NT && c[kt] != 0 && c[kt] != 2) ++kt;
+    return kt;
+  };
+  // global tile index base of (row j of item): K/V/Q tiles at (base + kt) * 8192
+  auto tile_base = [&](int item) -> unsigned long long {
+    const CoreItem ci = core_item(item, NT, G);
+    return ((((unsigned long long)ci.b * R) + ci.g0 + j) * HEADS + ci.h) * NT;
+  };
+  auto load_q = [&](unsigned long long tile) {
+    mbar_arrive_expect_tx(bar + B_QF + j, 8192);
+    bulk_g2s(smem + CG_SQ + j * 8192, args.ws + args.wl.off_q + tile * 8192, 8192, bar + B_QF + j);
+  };
+  auto load_k = [&](unsigned long long tile) {
+    mbar_arrive_expect_tx(bar + B_KF + j, 8192);
+    bulk_g2s(smem + CG_SK + j * 8192, args.ws + args.wl.off_k + tile * 8192, 8192, bar + B_KF + j);
+  };
+  auto load_v = [&](unsigned long long tile) {
+    mbar_arrive_expect_tx(bar + B_VF + j, 8192);
+    bulk_g2s(smem + CG_SV + j * 12288, args.ws + args.wl.off_v + tile * 8192, 8192, bar + B_VF + j);
+  };
+  // this warp is done reading the tri-bias stage of step (ii, kt); the last of the 16 warps refills
+  // that stage with step + NB
+  auto release_bias = [&](int ii, int kt) {
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      const int bs = (ii * NT + kt) % CG_NB;
+      if (atomicAdd(bias_cnt + bs, 1) == CG_SOFTMAX_WARPS - 1) {
+        bias_cnt[bs] = 0;
+        fence_proxy_async_smem();
+        int i3 = ii, k3 = kt + CG_NB;
+        while (k3 >= NT) { k3 -= NT; ++i3; }
+        load_bias(i3, k3, ii);
       }
-      mbar_wait(bar + B_QF + j, 0, status, DEV_TIMEOUT_TMA);
+    }
+    __syncwarp();
+  };
+
+  // the class word of the item two ahead, prefetched by the row's quad-0 warp (lane l: kt = 4l..4l+3)
+  uint32_t cls_pf = quad == 0 ? class_word(blockIdx.x + gridDim.x, j, lane) : 0u;
+  // first item: Q, K, V of the row's first active tile
+  if (leader) {
+    const int k0 = next_active(0, 0);
+    if (k0 < NT) {
+      const unsigned long long tb = tile_base(blockIdx.x);
+      load_q(tb + core_item(blockIdx.x, NT, G).qt);
+      load_k(tb + k0);
+      load_v(tb + k0);
+    }
+  }
+  int n = 0;   // active tiles processed by this row (all items): phase of KF/VF/SF/OF
+  int nq = 0;  // Q tiles consumed by this row: phase of QF (leader only)
+  int ii = 0;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++ii) {
+    const int cs = ii & 1;
+    // classes of the next item into slot cs ^ 1 (its last readers, item ii - 1, finished before the
+    // item barrier), then start loading those of the item after it
+    if (quad == 0) {
+      reinterpret_cast<uint32_t*>(scls + ((cs ^ 1) * CG_RG + j) * TILE)[lane] = cls_pf;
+      cls_pf = class_word(item + 2 * gridDim.x, j, lane);
+      __syncwarp();
+    }
+    if (leader) {
+      const int first = next_active(cs, 0), nf = next_active(cs ^ 1, 0);
+      rs->cur = tile_base(item);
+      rs->nxt_first = nf;
+      if (nf < NT) {
+        rs->nxt = tile_base(item + gridDim.x);
+        rs->nxt_qt = core_item(item + gridDim.x, NT, G).qt;
+      }
+      // a row without active tiles in this item fetches the next item's first tiles now
+      if (first == NT && nf < NT) {
+        load_q(rs->nxt + rs->nxt_qt);
+        load_k(rs->nxt + nf);
+        load_v(rs->nxt + nf);
+      }
+      if (first < NT) {
+        mbar_wait(bar + B_QF + j, nq & 1, status, DEV_TIMEOUT_TMA);
+        ++nq;
+      }
     }
 
-    // this warp is done reading tri-bias stage kt % NB; the last of the 16 warps refills it with kt + NB
-    auto release_bias = [&](int kt) {
-      __syncwarp();
-      if (lane == 0) {
-        __threadfence_block();
-        const int bs = kt % CG_NB;
-        if (atomicAdd(bias_cnt + bs, 1) == CG_SOFTMAX_WARPS - 1) {
-          bias_cnt[bs] = 0;
-          if (kt + CG_NB < NT) {
-            fence_proxy_async_smem();
-            load_bias(kt + CG_NB);
-          }
-        }
-      }
-      __syncwarp();
-    };
+    float o[C_HEAD], l = 0.f, m = 0.f;
+    bool started = false;
+#pragma unroll
+    for (int d = 0; d < C_HEAD; ++d) o[d] = 0.f;
+    const uint8_t* my_cls = scls + (cs * CG_RG + j) * TILE;
+
     for (int kt = 0; kt < NT; ++kt) {
-      const int bs = kt % CG_NB;
-      const int cls = scls[j * TILE + kt];
+      const int s = ii * NT + kt;  // step of the CTA's bias ring
+      const int bs = s % CG_NB;
+      const int cls = my_cls[kt];
       const bool act = cls == 0 || cls == 2;
       float alpha = 1.f;
-      if (act) {
-        // S = Q K^T, issued by this row's leader
-        if (leader) {
-          mbar_wait(bar + B_KF + j, n & 1, status, DEV_TIMEOUT_TMA);
-          tc_fence_after();
+      if (act && leader) {
+        // S = Q K^T
+        mbar_wait(bar + B_KF + j, n & 1, status, DEV_TIMEOUT_TMA);
+        tc_fence_after();
 #pragma unroll
-          for (int k2 = 0; k2 < C_HEAD / 16; ++k2) {
-            const uint64_t ad = smem_desc_noswizzle(smem_u32(smem + CG_SQ + j * 8192) + k2 * 256, 128, 512);
-            const uint64_t bd = smem_desc_noswizzle(smem_u32(smem + CG_SK + j * 8192) + k2 * 256, 128, 512);
-            umma_ss(buf0, ad, bd, idS, k2 > 0 ? 1u : 0u);
-          }
-          umma_commit(bar + B_SF + j);
+        for (int k2 = 0; k2 < C_HEAD / 16; ++k2) {
+          const uint64_t ad = smem_desc_noswizzle(smem_u32(smem + CG_SQ + j * 8192) + k2 * 256, 128, 512);
+          const uint64_t bd = smem_desc_noswizzle(smem_u32(smem + CG_SK + j * 8192) + k2 * 256, 128, 512);
+          umma_ss(buf0, ad, bd, idS, k2 > 0 ? 1u : 0u);
         }
+        umma_commit(bar + B_SF + j);
       }
-      mbar_wait(bar + B_BF + bs, (kt / CG_NB) & 1, status, DEV_TIMEOUT_TMA);
+      mbar_wait(bar + B_BF + bs, (s / CG_NB) & 1, status, DEV_TIMEOUT_TMA);
       if (act) {
         mbar_wait(bar + B_SF + j, n & 1, status, DEV_TIMEOUT_MMA);
         __syncwarp();
         tc_fence_after();
-        if (leader) {  // S has consumed the K slot: prefetch the row's next key tile
-          const int kn = next_active(kt + 1);
+        if (leader) {  // S has consumed the K slot (and, after the row's last tile, the Q slot)
+          const int kn = next_active(cs, kt + 1);
           if (kn < NT) {
-            mbar_arrive_expect_tx(bar + B_KF + j, 8192);
-            bulk_g2s(smem + CG_SK + j * 8192, args.ws + args.wl.off_k + (tile0 + kn) * 8192, 8192, bar + B_KF + j);
+            load_k(rs->cur + kn);
+          } else if (rs->nxt_first < NT) {
+            load_q(rs->nxt + rs->nxt_qt);
+            load_k(rs->nxt + rs->nxt_first);
           }
         }
         const unsigned char* tbp = smem + CG_SB + bs * 32768 + t * 16;
@@ -569,6 +674,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
 #pragma unroll
           for (int gq = 0; gq < 4; ++gq) bw[gq] = *reinterpret_cast<const uint4*>(tbp + (4 * c + gq) * 2048);
           tmem_ld_wait();
+          tmem_regs_ready(sr);
           float xs[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) xs[i] = __uint_as_float(sr[i]);
@@ -598,7 +704,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
           tmem_st32(buf + 32 * c, sr);
         }
         tmem_st_wait();
-        release_bias(kt);
+        release_bias(ii, kt);
         const float mx = fmaxf(max3f(mxa, mxb, mxc), mxd);
         // lazy rescale: keep the running maximum unless it grew by more than 8 (a factor 256)
         if (!started) {
@@ -616,6 +722,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
           uint32_t xr[32];
           tmem_ld32(buf + 32 * c, xr);
           tmem_ld_wait();
+          tmem_regs_ready(xr);
           uint32_t pk[16];
           // 10 of every 16 pairs on the MUFU, 6 on the FMA/ALU pipes (the split that balances the two)
 #pragma unroll
@@ -637,50 +744,51 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
           }
           umma_commit(bar + B_OF + j);
         }
-      } else {
-        release_bias(kt);
-      }
-      if (act) {
         mbar_wait(bar + B_OF + j, n & 1, status, DEV_TIMEOUT_MMA);
         __syncwarp();
         tc_fence_after();
-        if (leader) {  // P.V has consumed the V slot: prefetch the row's next value tile
-          const int kn = next_active(kt + 1);
-          if (kn < NT) {
-            mbar_arrive_expect_tx(bar + B_VF + j, 8192);
-            bulk_g2s(smem + CG_SV + j * 12288, args.ws + args.wl.off_v + (tile0 + kn) * 8192, 8192, bar + B_VF + j);
-          }
+        if (leader) {  // P.V has consumed the V slot
+          const int kn = next_active(cs, kt + 1);
+          if (kn < NT) load_v(rs->cur + kn);
+          else if (rs->nxt_first < NT) load_v(rs->nxt + rs->nxt_first);
         }
         uint32_t ov[32], lv[16];
         tmem_ld32(buf + 64, ov);
         tmem_ld16(buf + 96, lv);
         tmem_ld_wait();
+        tmem_regs_ready(ov);
+        tmem_regs_ready(lv);
 #pragma unroll
         for (int d = 0; d < C_HEAD; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(ov[d]));
         l = fmaf(l, alpha, __uint_as_float(lv[0]));
         tc_fence_before();
         wg_sync(j);  // the row's columns are free for the next S
         ++n;
+      } else {
+        release_bias(ii, kt);
       }
     }
 
     // ---- epilogue: o / l -> fp16 core image of (b, row, qt), channels h*32.. (the sigmoid gate is
     //      applied by the output projection, which streams the matching g tile) ----
-    if (row_ok) {
-      const int q = qt * TILE + t;
+    if (started) {
+      const CoreItem ci = core_item(item, NT, G);
+      const int q = ci.qt * TILE + t;
       const bool qvalid = q < N;
-      const int al = g0 + j;
       const float inv_l = 1.0f / l;
-      unsigned char* cimg = args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + qt) * 32768;
+      unsigned char* cimg = args.ws + args.wl.off_core + (((size_t)ci.b * R + ci.g0 + j) * NT + ci.qt) * 32768;
 #pragma unroll
       for (int d = 0; d < C_HEAD; d += 8) {
         uint32_t ow[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           ow[i] = qvalid ? H16<__half>::pack(o[d + 2 * i] * inv_l, o[d + 2 * i + 1] * inv_l) : 0u;
-        *reinterpret_cast<uint4*>(cimg + img_off(t, h * C_HEAD + d, HC)) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        *reinterpret_cast<uint4*>(cimg + img_off(t, ci.h * C_HEAD + d, HC)) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     }
+    // bias addressing of item ii + 2 (its slot last served item ii - 1, whose refills are all done)
+    if (tid == 0) iinfo[(ii + 2) % 3] = item_info(item + 2 * gridDim.x);
+    __syncthreads();  // item barrier: class slot cs and item-info slot ii % 3 are free again
   }
 
   tc_fence_before();
@@ -692,7 +800,8 @@ template <typename T>
 static cudaError_t core_tc_launch(const LayerArgs& a, cudaStream_t st) {
   cudaFuncSetAttribute(core_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, CG_SMEM);
   const int R = a.row_end - a.row_begin;
-  dim3 grid(a.wl.NT, (R + CG_RG - 1) / CG_RG, a.B * HEADS);
+  const int n_items = a.wl.NT * ((R + CG_RG - 1) / CG_RG) * a.B * HEADS;
+  const int grid = n_items < a.num_sms ? n_items : a.num_sms;
   core_tc_kernel<T><<<grid, CG_THREADS, CG_SMEM, st>>>(a);
   return cudaGetLastError();
 }

@@ -53,12 +53,13 @@ struct PackedLayout {
 //   g        : [B][R][N][128] 16-bit
 //   core_img : [B][R][NT] tiles of 32 KB (128 positions x 128 channels, K-major image)
 //   mb       : [B][R][Np] fp32, log2-domain mask bias; padded keys -1e30
-//   ts       : [B][R][NT] uint8 key-tile class: 0 all keys valid, 1 all masked (skip), 2 mixed
+//   ts       : [B][R][NTs] uint8 key-tile class: 0 all keys valid, 1 all masked (skip), 2 mixed;
+//              NTs = NT rounded up to 4 (one aligned 32-bit word per 4 tiles)
 // fp32 path:
 //   bias     : [N][B][H][Np] fp32 tri bias (natural units)
 //   q (pre-scaled by C^-1/2), k, v, g, core : [B][R][N][128] fp32;  mb : [B][R][Np] = inf * (mask - 1)
 struct Workspace {
-  int B, N, R, dtype, Np, NT;
+  int B, N, R, dtype, Np, NT, NTs;
   size_t off_q, off_k, off_v, off_g, off_core, off_bias, off_mb, off_ts, total;
 
   __host__ __device__ static Workspace make(int B, int N, int R, int dtype) {
@@ -66,6 +67,7 @@ struct Workspace {
     w.B = B; w.N = N; w.R = R; w.dtype = dtype;
     w.Np = round_tile(N);
     w.NT = w.Np / TILE;
+    w.NTs = (w.NT + 3) / 4 * 4;
     const size_t A = 256;
     size_t o = 0;
     w.off_bias = o;
@@ -86,7 +88,7 @@ struct Workspace {
       w.off_core = o; o = align_up(o + (size_t)B * R * w.NT * 32768, A);
     }
     w.off_mb = o; o = align_up(o + (size_t)B * R * w.Np * 4, A);
-    w.off_ts = o; o = align_up(o + (size_t)B * R * w.NT, A);
+    w.off_ts = o; o = align_up(o + (size_t)B * R * w.NTs, A);
     w.total = o;
     return w;
   }

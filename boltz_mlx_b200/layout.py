@@ -54,6 +54,7 @@ class Workspace:
     dtype: int
     Np: int = 0
     NT: int = 0
+    NTs: int = 0  # tile-class row stride: NT rounded up to 4
     off_q: int = 0
     off_k: int = 0
     off_v: int = 0
@@ -69,6 +70,7 @@ class Workspace:
         w = cls(B, N, R, dtype)
         w.Np = round_tile(N)
         w.NT = w.Np // TILE
+        w.NTs = (w.NT + 3) // 4 * 4
         o = 0
         # tri bias first: one fixed place for every row count (row chunks / ranks share it)
         w.off_bias = o
@@ -88,7 +90,7 @@ class Workspace:
             w.off_g = o; o = align(o + B * R * N * C_IN * 2)
             w.off_core = o; o = align(o + B * R * w.NT * 32768)
         w.off_mb = o; o = align(o + B * R * w.Np * 4)
-        w.off_ts = o; o = align(o + B * R * w.NT)
+        w.off_ts = o; o = align(o + B * R * w.NTs)
         w.total = o
         return w
 

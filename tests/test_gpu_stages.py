@@ -112,7 +112,7 @@ def test_tile_classes():
     mask[0, 2, :] = 0  # row 2: no valid key -> every tile kept
     ctx = run_ln_proj(N, "bf16", True, mask=mask)
     w, ws = ctx["w"], ctx["ws"]
-    ts = ws[w.off_ts:w.off_ts + N * w.NT].view(N, w.NT).cpu().tolist()
+    ts = ws[w.off_ts:w.off_ts + N * w.NTs].view(N, w.NTs)[:, :w.NT].cpu().tolist()
     assert w.NT == 3
     assert ts[0] == [0, 1, 2]  # the last tile holds padded keys -> mixed
     assert ts[1] == [2, 0, 2]
