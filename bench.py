@@ -37,6 +37,8 @@ CONFIGS = {
     0: dict(N=128, dtype="fp32", z_scale=1.0, pad="none", seed_z=0, seed_w=0, pair=False),
     1: dict(N=384, dtype="fp16", z_scale=1.0, pad="fixed38", seed_z=1, seed_w=1, pair=True),
     2: dict(N=1024, dtype="bf16", z_scale=0.5, pad="uniform15", seed_z=2, seed_w=2, pair=True),
+    # 64 pairformer-style blocks of start+end triangle attention = 128 layers, distinct weights per layer
+    3: dict(N=768, dtype="fp16", z_scale=1.0, pad="none", seed_z=3, seed_w=3, pair=True, blocks=64),
     4: dict(N=2048, dtype="bf16", z_scale=1.0, pad="frac05", seed_z=4, seed_w=4, pair=True),
 }
 
@@ -84,9 +86,92 @@ def make_config_inputs(cfg_id: int, N: int | None = None, B: int = 1):
     return z, pm, make_params(c["seed_w"]), make_params(c["seed_w"] + 100)
 
 
+def stack_params(cfg_id: int, n_layers: int) -> list:
+    """Distinct seeded weights for every layer of a stack (layer l: starting node when l is even)."""
+    return [make_params(1000 * CONFIGS[cfg_id]["seed_w"] + l) for l in range(n_layers)]
+
+
+class LayerStack:
+    """A stack of start/end triangle-attention layers with residual adds, run in place on a device z
+    through the C ABI (triattn_forward with add_residual=1), in one precision."""
+
+    def __init__(self, N: int, params: list, precision: str, device):
+        from boltz_mlx_b200 import _lib
+        from boltz_mlx_b200.triangle_attention import TriangleAttention, load_params
+
+        self.L, self.N, self.dt = _lib.lib(), N, _lib.dtype_code(precision)
+        self.packs = []
+        for l, p in enumerate(params):
+            m = TriangleAttention(starting=(l % 2 == 0), precision=precision).to(device)
+            load_params(m, {k: (v.to(device) if v is not None else None) for k, v in p.items()})
+            self.packs.append(m.packed_weights(self.dt))
+        self.wsb = _lib.workspace_bytes(1, N, N, self.dt)
+        self.work = torch.empty(self.wsb, dtype=torch.uint8, device=device)
+
+    def run(self, z, mask, stream):
+        from boltz_mlx_b200 import _lib
+
+        for l, pk in enumerate(self.packs):
+            _lib.check(self.L.triattn_forward(z.data_ptr(), mask.data_ptr(), pk.data_ptr(), 1, self.N, int(l % 2 == 0),
+                                              1e9, self.dt, 1, z.data_ptr(), self.work.data_ptr(), self.wsb, stream))
+
+
+def stack_drift(cfg_id: int = 3, N: int | None = None, blocks: int | None = None, steps: int = 3,
+                warmup: int = 1) -> dict:
+    """Config 3: the 16-bit stack timed (sustained ms per layer) and its final z compared with the same
+    stack run through the library's fp32 path (max_rel = max|d| / max|ref|, mean_abs, cos, and the same
+    on the accumulated update z_final - z_0)."""
+    from boltz_mlx_b200 import _lib
+
+    c = CONFIGS[cfg_id]
+    N = c["N"] if N is None else N
+    n_layers = 2 * (c["blocks"] if blocks is None else blocks)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    z0, pm, _, _ = make_config_inputs(cfg_id, N=N)
+    z0, pm = z0.to(dev), pm.to(dev)
+    params = stack_params(cfg_id, n_layers)
+    stream = torch.cuda.current_stream(dev)
+    s16 = LayerStack(N, params, c["dtype"], dev)
+    z = z0.clone()
+    for _ in range(warmup):
+        z.copy_(z0)
+        s16.run(z, pm, stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ms = 0.0
+    for _ in range(steps):
+        z.copy_(z0)
+        e0.record(stream)
+        s16.run(z, pm, stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms += e0.elapsed_time(e1)
+    ms_layer = ms / steps / n_layers
+    z16 = z.clone()
+    del s16
+    s32 = LayerStack(N, params, "fp32", dev)
+    z.copy_(z0)
+    s32.run(z, pm, stream.cuda_stream)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "device status word set"
+    z32 = z
+
+    def met(a, b):
+        d = (a - b).double()
+        bb = b.double()
+        cos = float((a.double() * bb).sum() / (a.double().norm() * bb.norm()))
+        return {"max_rel": float(d.abs().max() / bb.abs().max()), "mean_abs": float(d.abs().mean()), "cos": cos}
+
+    out = {"N": N, "layers": n_layers, "precision": c["dtype"], "ms_per_layer": ms_layer,
+           "z": met(z16, z32), "update": met(z16 - z0, z32 - z0),
+           "ref_abs_max": float(z32.abs().max()), "update_abs_mean": float((z32 - z0).abs().mean())}
+    return out
+
+
 # ---- clocks -------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi samples every 200 ms during the timed region (median SM clock, throttle reasons)."""
+    """nvidia-smi samples every 50 ms during the timed region (median SM clock, throttle reasons); the
+    timed region starts only after the first sample has arrived (nvidia-smi takes a moment to start)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -98,10 +183,14 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 3.0:
+                time.sleep(0.01)
+            self.rows.clear()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -375,6 +464,44 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+def run_stack(args):
+    """Config 3 line: sustained ms per layer of the 128-layer 16-bit stack and its drift against the
+    same stack through the fp32 path."""
+    torch.cuda.set_device(0)
+    r = stack_drift(args.config, steps=args.steps, warmup=args.warmup)
+    fl = layer_flops(r["N"])["total"]
+    line = {"metric": f"tri-attn ms/layer, {r['layers']}-layer start+end stack, N={r['N']}, {r['precision']} (config 3)",
+            "value": r["ms_per_layer"], "unit": "ms/layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "tflops": fl / (r["ms_per_layer"] * 1e-3) / 1e12, "dtype": r["precision"],
+            "data": "synthetic: z~N(0,1), mask ones, distinct seeded N(0,1/128) weights per layer",
+            "config": {"workload": f"config3: {r['layers']} layers, residual adds, N={r['N']}", "N": r["N"]},
+            "drift_vs_fp32_path": {"z": r["z"], "update": r["update"]}}
+    print(json.dumps(line), flush=True)
+
+
+def run_case(args):
+    """One start+end pair at N = args.case (bf16 unless --precision), for ncu captures of a small case."""
+    from boltz_mlx_b200 import _lib
+    from boltz_mlx_b200.triangle_attention import TriangleAttention, load_params
+
+    dev = torch.device("cuda", 0)
+    prec = args.precision or "bf16"
+    z, pm, ps, pe = make_config_inputs(2, N=args.case)
+    x, m = z.to(dev), pm.to(dev)
+    mods = []
+    for starting, p in ((True, ps), (False, pe)):
+        mod = TriangleAttention(starting=starting, precision=prec).to(dev)
+        load_params(mod, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
+        mods.append(mod)
+    for _ in range(2):
+        y = x.clone()
+        for mod in mods:
+            y = mod.forward_residual(y, m, inplace=True)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "device status word set"
+    print(json.dumps({"case": args.case, "precision": prec, "mean_abs": float(y.abs().mean())}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -384,10 +511,18 @@ def main():
     ap.add_argument("--config", type=int, default=None)
     ap.add_argument("--precision", default=None)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--case", type=int, default=None,
+                    help="profiling case: run one start+end pair at this N once (after one warm-up pair), "
+                         "check the device status and exit; nothing is timed")
     args = ap.parse_args()
+    if args.case is not None:
+        run_case(args)
+        return
     if args.config is None:
         args.config = 2  # one workload for every GPU count, so the driver's scaling ratios compare like with like
-    if args.impl == "reference":
+    if args.impl == "b200" and "blocks" in CONFIGS[args.config]:
+        run_stack(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)
