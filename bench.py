@@ -170,8 +170,9 @@ def stack_drift(cfg_id: int = 3, N: int | None = None, blocks: int | None = None
 
 # ---- clocks -------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi samples every 50 ms during the timed region (median SM clock, throttle reasons); the
-    timed region starts only after the first sample has arrived (nvidia-smi takes a moment to start)."""
+    """nvidia-smi samples every 50 ms around the timed region (median SM clock, throttle reasons): the
+    timed region starts once the first sample has arrived (taken right after the warm-up, at load
+    clocks), so even a short region carries a record."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -190,7 +191,6 @@ class ClockSampler:
             t0 = time.time()
             while not self.rows and time.time() - t0 < 3.0:
                 time.sleep(0.01)
-            self.rows.clear()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self

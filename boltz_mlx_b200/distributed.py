@@ -121,8 +121,10 @@ class ShardedPair:
         self.end(z_loc, mask, packed_end)
 
     def nvlink_bytes_per_pair(self) -> int:
-        """Bytes each rank sends over NVLink per pair: 2 bias all-gathers + 2 all-to-alls of fp32 z blocks."""
-        bias = (self.P - 1) * self.R * HEADS * self.w.Np * 4
+        """Bytes each rank sends over NVLink per pair: 2 tri-bias all-gathers (its own bias rows to each
+        of the P - 1 peers) + 2 all-to-alls of fp32 z blocks."""
+        b0, b1 = self.w.bias_rows(self.r0, self.r1)
+        bias = (self.P - 1) * (b1 - b0)
         a2a = (self.P - 1) * self.R * self.R * C_IN * 4
         return 2 * bias + 2 * a2a
 
@@ -150,12 +152,10 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
             m = TriangleAttention(starting=starting, precision=prec).to(dev)
             load_params(m, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
             packs.append(m.packed_weights(sp.dt))
-        z0 = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
         mask = pm_h[0].contiguous().to(dev)
-        z_loc = torch.empty_like(z0)
+        z_loc = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
 
-        def step():
-            z_loc.copy_(z0)
+        def step():  # in place: every step is the same work on the updated shard
             sp.pair(z_loc, mask, packs[0], packs[1])
 
         for _ in range(args.warmup):
@@ -179,6 +179,24 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         fl = layer_flops(N)
         pair_flops = 2 * fl["total"]
         value = pair_flops / (step_ms * 1e-3) / 1e12
+
+        # dominant kernel: the attention core on this rank's rows (end-layer workspace), timed alone;
+        # max over ranks
+        st = _lib.stream_handle(dev)
+        L = _lib.lib()
+        for _ in range(2):
+            _lib.check(L.triattn_core(1, N, sp.r0, sp.r1, sp.dt, sp.ws.data_ptr(), sp.ws.numel(), st))
+        ev0.record(stream)
+        for _ in range(5):
+            _lib.check(L.triattn_core(1, N, sp.r0, sp.r1, sp.dt, sp.ws.data_ptr(), sp.ws.numel(), st))
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        core = torch.tensor([ev0.elapsed_time(ev1) / 5], device=dev)
+        dist.all_reduce(core, op=dist.ReduceOp.MAX)
+        core_ms = float(core)
+        pk, pk_kind = peaks()
+        tensor_peak = pk.get("bf16_tflops", 1590.0)
+        achieved = fl["core"] * sp.R / N / (core_ms * 1e-3) / 1e12
 
         # e2e: host shard + mask copied in, shard copied out, every step
         zh = z_h[0, sp.r0:sp.r1].contiguous().pin_memory()
@@ -212,6 +230,11 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
                 "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
                 "config": workload_config(args.config, ws_n),
                 "nvlink_bytes_per_rank_per_step": sp.nvlink_bytes_per_pair(),
+                "roofline": {"bound": "tensor", "kernel": "core_tc (flash attention core, this rank's rows)",
+                             "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+                             "frac": achieved / tensor_peak, "peak_kind": f"{pk_kind} bf16 burst, per GPU",
+                             "traffic": None, "core_ms": core_ms,
+                             "algorithmic": f"F_core * R / N = {fl['core'] * sp.R / N:.4g} FLOP per launch"},
                 "e2e": {"value": pair_flops / (float(e2e) * 1e-3) / 1e12, "unit": "TFLOP/s",
                         "ms_per_step": float(e2e), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
                         "d2h_bytes_per_step": oh.numel() * 4 * ws_n},
