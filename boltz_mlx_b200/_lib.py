@@ -21,7 +21,7 @@ EXPORTED = [
     "triattn_version", "triattn_last_error_string", "triattn_device_status", "triattn_packed_weights_bytes",
     "triattn_pack_weights", "triattn_workspace_bytes", "triattn_forward", "triattn_mask_prep",
     "triattn_ln_proj", "triattn_core", "triattn_out_proj", "triattn_mask_prep_v", "triattn_ln_proj_v",
-    "triattn_out_proj_v",
+    "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb",
 ]
 
 
@@ -71,6 +71,9 @@ def lib() -> ctypes.CDLL:
         L.triattn_ln_proj_v.argtypes = [_vp, _l, _l, _l, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_out_proj_v.argtypes = [_vp, _l, _l, _l, _vp, _l, _l, _l, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz,
                                          _vp]
+        L.triattn_ln_proj_vb.argtypes = [_vp, _l, _l, _l, _i, _l, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+        L.triattn_out_proj_vb.argtypes = [_vp, _l, _l, _l, _i, _l, _vp, _l, _l, _l, _i, _l, _vp, _i, _i, _i, _i, _i,
+                                          _i, _vp, _sz, _vp]
         for name in EXPORTED:
             if name not in ("triattn_version", "triattn_last_error_string", "triattn_packed_weights_bytes",
                             "triattn_workspace_bytes"):

@@ -110,6 +110,8 @@ View pair_view(int N, int starting, int channels) {
   v.s_row = starting ? (long long)N * channels : channels;
   v.s_col = starting ? channels : (long long)N * channels;
   v.row0 = 0;
+  v.cblk = 0;
+  v.s_cblk = 0;
   return v;
 }
 
@@ -233,10 +235,17 @@ static int check_view(const char* name, const void* p, int64_t sb, int64_t sr, i
   return TRIATTN_OK;
 }
 
-static View make_view(int64_t sb, int64_t sr, int64_t sc, int row0) {
+static View make_view(int64_t sb, int64_t sr, int64_t sc, int row0, int cblk = 0, int64_t s_cblk = 0) {
   View v;
   v.s_batch = sb; v.s_row = sr; v.s_col = sc; v.row0 = row0;
+  v.cblk = cblk; v.s_cblk = s_cblk;
   return v;
+}
+
+static int check_blocks(const char* name, int N, int cblk, int64_t s_cblk) {
+  if (cblk < 0 || (cblk > 0 && (N % cblk || s_cblk < 0 || s_cblk % 4)))
+    return fail(TRIATTN_EINVAL, "%s: column blocks must divide N, with a non-negative stride of whole 16-byte rows", name);
+  return TRIATTN_OK;
 }
 
 int triattn_mask_prep_v(const float* mask, int64_t s_batch, int64_t s_row, int64_t s_col, int B, int N, float inf,
@@ -252,12 +261,20 @@ int triattn_mask_prep_v(const float* mask, int64_t s_batch, int64_t s_row, int64
 
 int triattn_ln_proj_v(const float* z, int64_t s_batch, int64_t s_row, int64_t s_col, const void* packed, int B, int N,
                       int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return triattn_ln_proj_vb(z, s_batch, s_row, s_col, 0, 0, packed, B, N, row_begin, row_end, dtype, workspace,
+                            workspace_bytes, stream);
+}
+
+int triattn_ln_proj_vb(const float* z, int64_t s_batch, int64_t s_row, int64_t s_col, int col_block, int64_t s_col_block,
+                       const void* packed, int B, int N, int row_begin, int row_end, int dtype, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   if (int r = check_dims(B, N, dtype)) return r;
   if (int r = check_rows(N, row_begin, row_end)) return r;
   if (int r = check_view("z", z, s_batch, s_row, s_col, true)) return r;
+  if (int r = check_blocks("z", N, col_block, s_col_block)) return r;
   if (int r = check_packed(packed, dtype)) return r;
   LayerArgs a = make_args(B, N, 1, row_begin, row_end, 0.f, z, nullptr, nullptr, 0, packed, workspace, dtype);
-  a.zv = make_view(s_batch, s_row, s_col, row_begin);
+  a.zv = make_view(s_batch, s_row, s_col, row_begin, col_block, s_col_block);
   if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
   if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -268,15 +285,27 @@ int triattn_out_proj_v(const float* z, int64_t zs_batch, int64_t zs_row, int64_t
                        int64_t os_batch, int64_t os_row, int64_t os_col, const void* packed, int B, int N,
                        int row_begin, int row_end, int dtype, int add_residual, void* workspace,
                        size_t workspace_bytes, void* stream) {
+  return triattn_out_proj_vb(z, zs_batch, zs_row, zs_col, 0, 0, out, os_batch, os_row, os_col, 0, 0, packed, B, N,
+                             row_begin, row_end, dtype, add_residual, workspace, workspace_bytes, stream);
+}
+
+int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, int z_col_block,
+                        int64_t zs_col_block, float* out, int64_t os_batch, int64_t os_row, int64_t os_col,
+                        int o_col_block, int64_t os_col_block, const void* packed, int B, int N, int row_begin,
+                        int row_end, int dtype, int add_residual, void* workspace, size_t workspace_bytes,
+                        void* stream) {
   if (int r = check_dims(B, N, dtype)) return r;
   if (int r = check_rows(N, row_begin, row_end)) return r;
   if (int r = check_view("out", out, os_batch, os_row, os_col, true)) return r;
-  if (add_residual)
+  if (int r = check_blocks("out", N, o_col_block, os_col_block)) return r;
+  if (add_residual) {
     if (int r = check_view("z", z, zs_batch, zs_row, zs_col, true)) return r;
+    if (int r = check_blocks("z", N, z_col_block, zs_col_block)) return r;
+  }
   if (int r = check_packed(packed, dtype)) return r;
   LayerArgs a = make_args(B, N, 1, row_begin, row_end, 0.f, z, nullptr, out, add_residual, packed, workspace, dtype);
-  a.zv = make_view(zs_batch, zs_row, zs_col, row_begin);
-  a.ov = make_view(os_batch, os_row, os_col, row_begin);
+  a.zv = make_view(zs_batch, zs_row, zs_col, row_begin, z_col_block, zs_col_block);
+  a.ov = make_view(os_batch, os_row, os_col, row_begin, o_col_block, os_col_block);
   if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
   if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

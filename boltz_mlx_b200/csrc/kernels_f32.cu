@@ -80,7 +80,7 @@ __global__ void mask_prep_kernel(const float* __restrict__ mask, View mv, int B,
   const int a = row_begin + al;
   float v;
   if (k < N) {
-    const float m = mask ? mask[b * mv.s_batch + (long long)(a - mv.row0) * mv.s_row + (long long)k * mv.s_col] : 1.0f;
+    const float m = mask ? mask[b * mv.s_batch + (long long)(a - mv.row0) * mv.s_row + view_col(mv, k)] : 1.0f;
     v = inf * (m - 1.0f);
     if (log2_domain) v *= LOG2E;
   } else {
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256) ln_proj_f32_kernel(LayerArgs args) {
     float4 xn = make_float4(0.f, 0.f, 0.f, 0.f);
     if (c < N) {
       const float* x = args.z + b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row +
-                       (long long)c * args.zv.s_col;
+                       view_col(args.zv, c);
       const float4 v = reinterpret_cast<const float4*>(x)[lane];
       const float mean = warp_sum(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
       const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
@@ -351,11 +351,11 @@ __global__ void __launch_bounds__(256) out_proj_f32_kernel(LayerArgs args) {
       const int c = c0 + ty * 4 + i;
       if (c >= N) continue;
       const long long off = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row +
-                            (long long)c * args.ov.s_col + o0 + tx * 4;
+                            view_col(args.ov, c) + o0 + tx * 4;
       float4 r = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
       if (args.add_residual) {
         const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row +
-                               (long long)c * args.zv.s_col + o0 + tx * 4;
+                               view_col(args.zv, c) + o0 + tx * 4;
         const float4 zz = *reinterpret_cast<const float4*>(args.z + zoff);
         r.x += zz.x; r.y += zz.y; r.z += zz.z; r.w += zz.w;
       }

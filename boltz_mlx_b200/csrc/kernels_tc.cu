@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int c = ct * TILE + warp * 8 + i;
-      xv[i] = c < N ? __ldcs(reinterpret_cast<const float4*>(zr + (long long)c * args.zv.s_col) + lane)
+      xv[i] = c < N ? __ldcs(reinterpret_cast<const float4*>(zr + view_col(args.zv, c)) + lane)
                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(128) mask_prep_tc_kernel(LayerArgs args) {
     float v = -1e30f;
     if (k < N) {
       const float m =
-          args.mask ? args.mask[b * mv.s_batch + (long long)(a - mv.row0) * mv.s_row + (long long)k * mv.s_col] : 1.0f;
+          args.mask ? args.mask[b * mv.s_batch + (long long)(a - mv.row0) * mv.s_row + view_col(mv, k)] : 1.0f;
       v = args.inf * (m - 1.0f) * LOG2E;
     }
     mb[k] = v;
@@ -888,9 +888,9 @@ __global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs ar
   const int quad = warp & 3, part = warp >> 2;
   const int c = ct * TILE + quad * 32 + lane;
   const bool valid = c < N;
-  const long long ooff = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row + (long long)c * args.ov.s_col +
+  const long long ooff = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row + view_col(args.ov, c) +
                          64 * part;
-  const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row + (long long)c * args.zv.s_col +
+  const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row + view_col(args.zv, c) +
                          64 * part;
   // all 16 residual float4 of this thread in flight before the MMA wait (out may alias z, so every
   // load is issued before the first store)

@@ -106,12 +106,21 @@ __host__ __device__ __forceinline__ uint32_t vimg_off(uint32_t key, uint32_t ch)
 }
 
 // Attention-oriented view of a [B][N][N][ch] tensor: element (b, a, c, ch) lives at
-//   base + b * s_batch + (a - row0) * s_row + c * s_col + ch
-// (starting node: s_row = N*ch, s_col = ch; ending node: s_row = ch, s_col = N*ch).
+//   base + b * s_batch + (a - row0) * s_row + col(c) + ch,
+//   col(c) = c * s_col                                         (cblk = 0)
+//          = (c / cblk) * s_cblk + (c % cblk) * s_col           (columns in blocks of cblk)
+// (starting node: s_row = N*ch, s_col = ch; ending node: s_row = ch, s_col = N*ch; a row-sharded
+// residual stream kept as [P][rows][cols of rank p][ch] blocks: s_row = cblk*ch, s_col = ch,
+// s_cblk = rows*cblk*ch).
 struct View {
   long long s_batch, s_row, s_col;
   int row0;
+  int cblk;
+  long long s_cblk;
 };
+__host__ __device__ __forceinline__ long long view_col(const View& v, int c) {
+  return v.cblk ? (long long)(c / v.cblk) * v.s_cblk + (long long)(c % v.cblk) * v.s_col : (long long)c * v.s_col;
+}
 
 struct LayerArgs {
   int B, N, row_begin, row_end;

@@ -8,9 +8,14 @@ multi-GPU form distributes those row chunks:
 * Starting node: LN + projection of the local rows, their tri-bias rows, ONE all-gather of the tri
   bias ([N][B][H][Np] fp32, rows contiguous), local attention core and output projection + residual.
 * Ending node: attention row a is column a of z, so the pair tensor is re-sharded by columns with
-  an all-to-all (rows_to_cols), the same stages run on the column block through strided views
-  (no transposed copy of z is materialised by the kernels), the tri bias is all-gathered, and the
-  updated column block goes back to row sharding with a second all-to-all (cols_to_rows).
+  an all-to-all, the same stages run on the column block through strided views (no transposed copy
+  of z is materialised by the kernels), the tri bias is all-gathered, and the updated column block
+  goes back to row sharding with a second all-to-all.
+* Block layout of the residual stream: a rank keeps its rows of z as [P][R][R][C] blocks (block p =
+  the columns of rank p).  The starting node runs on it through a column-blocked view; block p is
+  exactly the chunk all_to_all_single sends to rank p, and the ending node's column block, sent
+  back, lands in the same layout.  So a start+end pair (pair_blocks) costs two all-to-alls and no
+  transposing copy.  pair() wraps it for callers that hold row-layout shards [R][N][C].
 
 The exchange steps are plain torch.distributed collectives, so the host logic also runs on CPU
 ranks with the gloo backend (tests/test_distributed_cpu.py).
@@ -60,6 +65,35 @@ def cols_to_rows(zt: torch.Tensor, P: int, recv: torch.Tensor, z_loc_out: torch.
     N, R, Cc = zt.shape
     dist.all_to_all_single(recv, zt.reshape(P, R, R, Cc).contiguous(), group=group)
     z_loc_out.view(R, P, R, Cc).copy_(recv.transpose(0, 1))
+
+
+def to_blocks(z_loc: torch.Tensor, P: int, z_blk: torch.Tensor) -> torch.Tensor:
+    """Row shard [R, N, C] -> block layout [P, R, R, C] (z_blk[p, i, a] = z_loc[i, p*R + a])."""
+    R, N, Cc = z_loc.shape
+    z_blk.copy_(z_loc.view(R, P, R, Cc).transpose(0, 1))
+    return z_blk
+
+
+def from_blocks(z_blk: torch.Tensor, z_loc: torch.Tensor) -> torch.Tensor:
+    """Block layout [P, R, R, C] -> row shard [R, N, C] (inverse of to_blocks)."""
+    P, R, _, Cc = z_blk.shape
+    z_loc.view(R, P, R, Cc).copy_(z_blk.transpose(0, 1))
+    return z_loc
+
+
+def blocks_to_cols(z_blk: torch.Tensor, recv: torch.Tensor, group=None) -> torch.Tensor:
+    """Block layout [P, R, R, C] of my rows -> column block [N, R, C] of my columns (all-to-all:
+    block p goes to rank p as-is).  recv is a [P, R, R, C] buffer; returns it viewed as [N, R, C]."""
+    P, R, _, Cc = z_blk.shape
+    dist.all_to_all_single(recv, z_blk, group=group)
+    return recv.view(P * R, R, Cc)
+
+
+def cols_to_blocks(zt: torch.Tensor, z_blk: torch.Tensor, group=None) -> None:
+    """Column block [N, R, C] -> block layout [P, R, R, C] of my rows (all-to-all; rows p*R.. of zt
+    go to rank p, which receives them as its block of my columns)."""
+    P, R, _, Cc = z_blk.shape
+    dist.all_to_all_single(z_blk, zt.view(P, R, R, Cc), group=group)
 
 
 class ShardedPair:
@@ -116,9 +150,48 @@ class ShardedPair:
                                         packed.data_ptr(), 1, N, r0, r1, dt, 1, ws, nb, st))
         cols_to_rows(zt, self.P, self.recv2, z_loc, self.group)
 
+    def start_blocks(self, z_blk: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
+        """z_blk [P, R, R, 128] (my rows of z, column blocks) += TriAttStart(z) for those rows, in place."""
+        L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
+        ws, nb = self.ws.data_ptr(), self.ws.numel()
+        mptr = None if mask is None else mask.data_ptr() + r0 * N * 4
+        _lib.check(L.triattn_mask_prep_v(mptr, N * N, N, 1, 1, N, self.inf, r0, r1, dt, ws, nb, st))
+        zp = z_blk.data_ptr()
+        s_row, s_col, cb, s_cb = R * C_IN, C_IN, R, R * R * C_IN
+        _lib.check(L.triattn_ln_proj_vb(zp, N * N * C_IN, s_row, s_col, cb, s_cb, packed.data_ptr(), 1, N, r0, r1, dt,
+                                        ws, nb, st))
+        gather_bias(self.ws, self.w, r0, r1, self.group)
+        _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
+        _lib.check(L.triattn_out_proj_vb(zp, N * N * C_IN, s_row, s_col, cb, s_cb, zp, N * N * C_IN, s_row, s_col, cb,
+                                         s_cb, packed.data_ptr(), 1, N, r0, r1, dt, 1, ws, nb, st))
+
+    def end_blocks(self, z_blk: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
+        """z_blk += TriAttEnd(z) for my rows: all-to-all to my column block, the layer on it in place,
+        all-to-all straight back into z_blk."""
+        L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
+        ws, nb = self.ws.data_ptr(), self.ws.numel()
+        zt = blocks_to_cols(z_blk, self.recv, self.group)  # [N, R, 128]
+        mptr = None if mask is None else mask.data_ptr() + r0 * 4
+        _lib.check(L.triattn_mask_prep_v(mptr, N * N, 1, N, 1, N, self.inf, r0, r1, dt, ws, nb, st))
+        zp = zt.data_ptr()
+        _lib.check(L.triattn_ln_proj_v(zp, N * R * C_IN, C_IN, R * C_IN, packed.data_ptr(), 1, N, r0, r1, dt, ws, nb,
+                                       st))
+        gather_bias(self.ws, self.w, r0, r1, self.group)
+        _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
+        _lib.check(L.triattn_out_proj_v(zp, N * R * C_IN, C_IN, R * C_IN, zp, N * R * C_IN, C_IN, R * C_IN,
+                                        packed.data_ptr(), 1, N, r0, r1, dt, 1, ws, nb, st))
+        cols_to_blocks(zt, z_blk, self.group)
+
+    def pair_blocks(self, z_blk, mask, packed_start, packed_end) -> None:
+        """One start+end pair on the block-layout residual stream (two all-to-alls, no copies)."""
+        self.start_blocks(z_blk, mask, packed_start)
+        self.end_blocks(z_blk, mask, packed_end)
+
     def pair(self, z_loc, mask, packed_start, packed_end) -> None:
-        self.start(z_loc, mask, packed_start)
-        self.end(z_loc, mask, packed_end)
+        """One start+end pair on a row-layout shard z_loc [R, N, 128] (converted to blocks and back)."""
+        to_blocks(z_loc, self.P, self.send)
+        self.pair_blocks(self.send, mask, packed_start, packed_end)
+        from_blocks(self.send, z_loc)
 
     def nvlink_bytes_per_pair(self) -> int:
         """Bytes each rank sends over NVLink per pair: 2 tri-bias all-gathers (its own bias rows to each
@@ -154,9 +227,11 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
             packs.append(m.packed_weights(sp.dt))
         mask = pm_h[0].contiguous().to(dev)
         z_loc = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
+        # the residual stream stays in block layout across steps (the layout the exchange uses)
+        z_blk = to_blocks(z_loc, sp.P, torch.empty(sp.P, sp.R, sp.R, C_IN, device=dev))
 
         def step():  # in place: every step is the same work on the updated shard
-            sp.pair(z_loc, mask, packs[0], packs[1])
+            sp.pair_blocks(z_blk, mask, packs[0], packs[1])
 
         for _ in range(args.warmup):
             step()
@@ -203,7 +278,7 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         mh = pm_h[0].contiguous().pin_memory()
         oh = torch.empty_like(zh).pin_memory()
 
-        def e2e_step():
+        def e2e_step():  # host row shard in, host row shard out (block conversion on the device)
             z_loc.copy_(zh, non_blocking=True)
             mask.copy_(mh, non_blocking=True)
             sp.pair(z_loc, mask, packs[0], packs[1])

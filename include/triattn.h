@@ -138,6 +138,21 @@ TRIATTN_API int triattn_out_proj_v(const float* z, int64_t zs_batch, int64_t zs_
                                    int row_begin, int row_end, int dtype, int add_residual, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/* Column-blocked views (no reference counterpart: the layout of a row-sharded residual stream).
+ * Column c of the view lives at (c / col_block)*s_col_block + (c % col_block)*s_col instead of
+ * c*s_col (col_block = 0: plain view).  A rank owning rows [r0, r0 + R) keeps its rows of z as
+ * [P][R][R][128] blocks (block p = columns of rank p): s_row = R*128, s_col = 128, col_block = R,
+ * s_col_block = R*R*128.  Block p is then exactly what all_to_all_single sends to rank p, and what
+ * comes back from the ending node lands in the same layout: the exchange needs no transposing copy. */
+TRIATTN_API int triattn_ln_proj_vb(const float* z, int64_t s_batch, int64_t s_row, int64_t s_col, int col_block,
+                                   int64_t s_col_block, const void* packed, int B, int N, int row_begin, int row_end,
+                                   int dtype, void* workspace, size_t workspace_bytes, void* stream);
+TRIATTN_API int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col,
+                                    int z_col_block, int64_t zs_col_block, float* out, int64_t os_batch,
+                                    int64_t os_row, int64_t os_col, int o_col_block, int64_t os_col_block,
+                                    const void* packed, int B, int N, int row_begin, int row_end, int dtype,
+                                    int add_residual, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Output projection (+ residual) of rows [row_begin,row_end), written in z's orientation. */
 TRIATTN_API int triattn_out_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
                      int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,

@@ -10,7 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from boltz_mlx_b200.distributed import cols_to_rows, gather_bias, rows_to_cols, shard_rows
+from boltz_mlx_b200.distributed import (blocks_to_cols, cols_to_blocks, cols_to_rows, from_blocks, gather_bias,
+                                        rows_to_cols, shard_rows, to_blocks)
 from boltz_mlx_b200.layout import Workspace
 
 
@@ -43,6 +44,17 @@ def _worker(rank, P, port, N, errq):
         for q in range(P):
             ref[:, q * R:(q + 1) * R] += float(q)
         assert torch.equal(out, ref[r0:r1]), "cols_to_rows"
+        # block layout of the residual stream: z_blk[p, i, a] = z[r0 + i, p*R + a]; the all-to-all
+        # sends block p to rank p as-is and the column block comes back into the same layout
+        z_blk = to_blocks(z_loc, P, torch.empty(P, R, R, C))
+        for q in range(P):
+            assert torch.equal(z_blk[q], z[r0:r1, q * R:(q + 1) * R]), "to_blocks"
+        assert torch.equal(from_blocks(z_blk, torch.empty_like(z_loc)), z_loc), "from_blocks"
+        zt2 = blocks_to_cols(z_blk, torch.empty(P, R, R, C))
+        assert torch.equal(zt2, z[:, r0:r1]), "blocks_to_cols"
+        zt2.mul_(2.0).add_(float(rank))
+        cols_to_blocks(zt2, z_blk)
+        assert torch.equal(from_blocks(z_blk, torch.empty_like(z_loc)), ref[r0:r1]), "cols_to_blocks"
         # tri-bias all-gather over the workspace layout
         for dtype in (0, 2):
             if dtype != 0 and R % 128:
