@@ -21,7 +21,7 @@ EXPORTED = [
     "triattn_version", "triattn_last_error_string", "triattn_device_status", "triattn_packed_weights_bytes",
     "triattn_pack_weights", "triattn_workspace_bytes", "triattn_forward", "triattn_mask_prep",
     "triattn_ln_proj", "triattn_core", "triattn_out_proj", "triattn_mask_prep_v", "triattn_ln_proj_v",
-    "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb",
+    "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb", "triattn_forward_fused",
 ]
 
 
@@ -62,6 +62,8 @@ def lib() -> ctypes.CDLL:
         L.triattn_workspace_bytes.restype = _sz
         L.triattn_workspace_bytes.argtypes = [_i, _i, _i, _i]
         L.triattn_forward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _vp, _sz, _vp]
+        L.triattn_forward_fused.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _i, _vp, _vp, _vp, _i,
+                                            _vp, _sz, _vp]
         L.triattn_mask_prep.argtypes = [_vp, _i, _i, _i, _f, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_ln_proj.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_core.argtypes = [_i, _i, _i, _i, _i, _vp, _sz, _vp]

@@ -128,6 +128,9 @@ LayerArgs make_args(int B, int N, int starting, int row_begin, int row_end, floa
   a.wl = Workspace::make(B, N, row_end - row_begin, dtype);
   a.status = device_status_ptr();
   a.num_sms = device_sm_count();
+  a.xn = nullptr;
+  a.ln_next_w = a.ln_next_b = nullptr;
+  a.ln_out = nullptr;
   return a;
 }
 
@@ -310,6 +313,47 @@ int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs_row, int64_
   if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return finish(dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st), "out_proj_v");
+}
+
+int triattn_forward_fused(const float* z, const void* xn, const float* mask, const void* packed, int B, int N,
+                          int starting, float inf, int dtype, int add_residual, float* out, int out_attn_layout,
+                          const float* ln_next_w, const float* ln_next_b, void* ln_out, int ln_out_swapped,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if ((xn || ln_out) && dtype == DT_F32)
+    return fail(TRIATTN_EUNSUPPORTED, "xn / ln_out belong to the 16-bit path (the reference's f16 pair block)");
+  if (!out || !aligned(out, 16)) return fail(TRIATTN_EINVAL, "out must be a 16-byte aligned device pointer");
+  if ((add_residual || !xn) && (!z || !aligned(z, 16)))
+    return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer (residual or LayerNorm input)");
+  if (xn && !aligned(xn, 16)) return fail(TRIATTN_EINVAL, "xn must be 16-byte aligned");
+  if (ln_out && (!aligned(ln_out, 16) || !ln_next_w || !ln_next_b || !aligned(ln_next_w, 16) || !aligned(ln_next_b, 16)))
+    return fail(TRIATTN_EINVAL, "ln_out needs 16-byte aligned ln_out, ln_next_w and ln_next_b");
+  if (int r = check_packed(packed, dtype)) return r;
+  LayerArgs a = make_args(B, N, starting, 0, N, inf, z, mask, out, add_residual, packed, workspace, dtype);
+  if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
+  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  if (xn) {
+    a.xn = xn;
+    a.xnv = pair_view(N, 1, C_IN);  // the layer's attention orientation (ending node: already transposed)
+  }
+  if (out_attn_layout) a.ov = pair_view(N, 1, C_IN);
+  if (ln_out) {
+    a.ln_next_w = ln_next_w;
+    a.ln_next_b = ln_next_b;
+    a.ln_out = ln_out;
+    // z's orientation seen from this layer, or with the two N axes swapped
+    a.lnv = pair_view(N, ln_out_swapped ? !starting : starting, C_IN);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_mask_prep(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "mask_prep");
+  e = dtype == DT_F32 ? launch_ln_proj_f32(a, st) : launch_ln_proj_tc(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "ln_proj");
+  e = dtype == DT_F32 ? launch_core_f32(a, st) : launch_core_tc(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "core");
+  e = dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "out_proj");
+  return TRIATTN_OK;
 }
 
 int triattn_forward(const float* z, const float* mask, const void* packed, int B, int N, int starting, float inf,

@@ -52,7 +52,7 @@ constexpr int LP_W_BYTES = NPROJ * C_IN * 2;  // 131072
 constexpr int LP_A_BYTES = TILE * C_IN * 2;   // 32768
 constexpr int LP_SMEM = LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4 + 64;
 
-template <typename T>
+template <typename T, bool XN>
 __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sW = smem;
@@ -98,8 +98,24 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
 #pragma unroll
   for (int hh = 0; hh < HEADS; ++hh) wb[hh] = reinterpret_cast<const float4*>(P + PackedLayout::w_b / 4 + hh * C_IN)[lane];
   // this warp's 8 z rows of a tile (zeros past N)
+  // caller-given LayerNorm output (16-bit, this layer's type): the LN is skipped and its bits become
+  // the operand image as they are (kernel-uniform)
+  constexpr bool xn_mode = XN;
   auto load_rows = [&](int tile, float4 (&xv)[8]) {
     const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+    if constexpr (xn_mode) {
+      // lane: 4 channels = 8 bytes, kept in .x/.y
+      const uint16_t* xr = reinterpret_cast<const uint16_t*>(args.xn) + b * args.xnv.s_batch +
+                           (long long)(args.row_begin + al - args.xnv.row0) * args.xnv.s_row;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = ct * TILE + warp * 8 + i;
+        const uint2 u = c < N ? __ldcs(reinterpret_cast<const uint2*>(xr + view_col(args.xnv, c)) + lane)
+                              : make_uint2(0u, 0u);
+        xv[i] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), 0.f, 0.f);
+      }
+      return;
+    }
     const float* zr = args.z + b * args.zv.s_batch + (long long)(args.row_begin + al - args.zv.row0) * args.zv.s_row;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -122,15 +138,22 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
     for (int i = 0; i < 8; ++i) {
       const int r = warp * 8 + i;
       const float4 v = xv[i];
-      const float mean = warp_sum32(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
-      const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
-      const float var = warp_sum32(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / C_IN);
-      const float rstd = rsqrtf(var + LN_EPS);
-      const float n0 = d0 * rstd * lw.x + lb.x, n1 = d1 * rstd * lw.y + lb.y;
-      const float n2 = d2 * rstd * lw.z + lb.z, n3 = d3 * rstd * lw.w + lb.w;
+      float n0, n1, n2, n3;
       uint2 pk;
-      pk.x = H16<T>::pack(n0, n1);
-      pk.y = H16<T>::pack(n2, n3);
+      if constexpr (xn_mode) {
+        pk = make_uint2(__float_as_uint(v.x), __float_as_uint(v.y));
+        const float2 a01 = H16<T>::unpack(pk.x), a23 = H16<T>::unpack(pk.y);
+        n0 = a01.x; n1 = a01.y; n2 = a23.x; n3 = a23.y;
+      } else {
+        const float mean = warp_sum32(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
+        const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+        const float var = warp_sum32(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / C_IN);
+        const float rstd = rsqrtf(var + LN_EPS);
+        n0 = d0 * rstd * lw.x + lb.x; n1 = d1 * rstd * lw.y + lb.y;
+        n2 = d2 * rstd * lw.z + lb.z; n3 = d3 * rstd * lw.w + lb.w;
+        pk.x = H16<T>::pack(n0, n1);
+        pk.y = H16<T>::pack(n2, n3);
+      }
       // swizzled image: one row's 256 bytes are two 128-byte runs (no bank conflicts)
       *reinterpret_cast<uint2*>(sA + sw128_off(r, 4 * lane, LP_A_BYTES / 2)) = pk;
       // four head sums at once: exchange halves (xor 16: heads 0,1 | 2,3; xor 8: one head each), then
@@ -257,17 +280,18 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
-template <typename T>
+template <typename T, bool XN>
 static cudaError_t ln_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
-  cudaFuncSetAttribute(ln_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM);
+  cudaFuncSetAttribute(ln_proj_tc_kernel<T, XN>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM);
   const int ntiles = a.wl.NT * (a.row_end - a.row_begin) * a.B;
   const int grid = ntiles < a.num_sms ? ntiles : a.num_sms;
-  ln_proj_tc_kernel<T><<<grid, LP_THREADS, LP_SMEM, st>>>(a);
+  ln_proj_tc_kernel<T, XN><<<grid, LP_THREADS, LP_SMEM, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
-  return dtype == DT_BF16 ? ln_proj_tc_launch<__nv_bfloat16>(a, st) : ln_proj_tc_launch<__half>(a, st);
+  if (a.xn) return dtype == DT_BF16 ? ln_proj_tc_launch<__nv_bfloat16, true>(a, st) : ln_proj_tc_launch<__half, true>(a, st);
+  return dtype == DT_BF16 ? ln_proj_tc_launch<__nv_bfloat16, false>(a, st) : ln_proj_tc_launch<__half, false>(a, st);
 }
 
 // =================================================================================================
@@ -819,7 +843,7 @@ cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 constexpr int OP_THREADS = 256;
 constexpr int OP_SMEM = 65536 + 64;
 
-template <typename T>
+template <typename T, bool LN_NEXT>
 __global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
@@ -903,19 +927,80 @@ __global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs ar
   mbar_wait(bars + 1, 0, status, DEV_TIMEOUT_MMA);
   __syncwarp();
   tc_fence_after();
-#pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
+  // y (+ residual) for 32 output channels of this thread's row: TMEM columns 64 part + 32 h2 ..
+  auto y_chunk = [&](int h2, float4 (&y)[8]) {
     uint32_t acc[32];
     tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
     tmem_ld_wait();
     tmem_regs_ready(acc);
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      const float4 zd = zz[8 * h2 + d];
+      y[d] = make_float4(__uint_as_float(acc[4 * d]) + zd.x, __uint_as_float(acc[4 * d + 1]) + zd.y,
+                         __uint_as_float(acc[4 * d + 2]) + zd.z, __uint_as_float(acc[4 * d + 3]) + zd.w);
+    }
+  };
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    float4 y[8];
+    y_chunk(h2, y);
     if (valid) {
 #pragma unroll
+      for (int d = 0; d < 8; ++d) __stcs(reinterpret_cast<float4*>(args.out + ooff) + 8 * h2 + d, y[d]);
+    }
+  }
+  if constexpr (LN_NEXT) {
+    // the next module's LayerNorm of the output rows (reference linear_addln, kernels_nax3.py:69-198):
+    // two-pass fp32 statistics over the row's 128 channels, whose halves live in threads (quad, lane)
+    // of parts 0 and 1; partial sums meet in shared memory (the operand images are free by now)
+    float* red = reinterpret_cast<float*>(sA);  // [2 statistics][2 parts][128 rows]
+    const int row = quad * 32 + lane;
+    float s1 = 0.f;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      float4 y[8];
+      y_chunk(h2, y);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) s1 += (y[d].x + y[d].y) + (y[d].z + y[d].w);
+    }
+    red[part * TILE + row] = s1;
+    __syncthreads();
+    const float mean = (red[row] + red[TILE + row]) * (1.0f / C_IN);
+    float s2 = 0.f;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      float4 y[8];
+      y_chunk(h2, y);
+#pragma unroll
       for (int d = 0; d < 8; ++d) {
-        const float4 zd = zz[8 * h2 + d];
-        const float4 y = make_float4(__uint_as_float(acc[4 * d]) + zd.x, __uint_as_float(acc[4 * d + 1]) + zd.y,
-                                     __uint_as_float(acc[4 * d + 2]) + zd.z, __uint_as_float(acc[4 * d + 3]) + zd.w);
-        __stcs(reinterpret_cast<float4*>(args.out + ooff) + 8 * h2 + d, y);
+        const float d0 = y[d].x - mean, d1 = y[d].y - mean, d2 = y[d].z - mean, d3 = y[d].w - mean;
+        s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+      }
+    }
+    red[2 * TILE + part * TILE + row] = s2;
+    __syncthreads();
+    const float rstd = rsqrtf((red[2 * TILE + row] + red[3 * TILE + row]) * (1.0f / C_IN) + LN_EPS);
+    {
+      uint16_t* lo = reinterpret_cast<uint16_t*>(args.ln_out) + b * args.lnv.s_batch +
+                     (long long)(a - args.lnv.row0) * args.lnv.s_row + view_col(args.lnv, c) + 64 * part;
+      const float4* lw4 = reinterpret_cast<const float4*>(args.ln_next_w + 64 * part);
+      const float4* lb4 = reinterpret_cast<const float4*>(args.ln_next_b + 64 * part);
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float4 y[8];
+        y_chunk(h2, y);  // warp-collective TMEM load: every lane, valid row or not
+        if (!valid) continue;
+#pragma unroll
+        for (int d = 0; d < 8; d += 2) {
+          const float4 w0 = __ldg(lw4 + 8 * h2 + d), w1 = __ldg(lw4 + 8 * h2 + d + 1);
+          const float4 c0 = __ldg(lb4 + 8 * h2 + d), c1 = __ldg(lb4 + 8 * h2 + d + 1);
+          uint4 pk;
+          pk.x = H16<T>::pack((y[d].x - mean) * rstd * w0.x + c0.x, (y[d].y - mean) * rstd * w0.y + c0.y);
+          pk.y = H16<T>::pack((y[d].z - mean) * rstd * w0.z + c0.z, (y[d].w - mean) * rstd * w0.w + c0.w);
+          pk.z = H16<T>::pack((y[d + 1].x - mean) * rstd * w1.x + c1.x, (y[d + 1].y - mean) * rstd * w1.y + c1.y);
+          pk.w = H16<T>::pack((y[d + 1].z - mean) * rstd * w1.z + c1.z, (y[d + 1].w - mean) * rstd * w1.w + c1.w);
+          *reinterpret_cast<uint4*>(lo + 32 * h2 + 4 * d) = pk;
+        }
       }
     }
   }
@@ -924,17 +1009,19 @@ __global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs ar
   if (warp == 0) tmem_dealloc(tbase, 128);
 }
 
-template <typename T>
+template <typename T, bool LN_NEXT>
 static cudaError_t out_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
-  cudaFuncSetAttribute(out_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
+  cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
   const int R = a.row_end - a.row_begin;
   dim3 grid(a.wl.NT, R, a.B);
-  out_proj_tc_kernel<T><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
+  out_proj_tc_kernel<T, LN_NEXT><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_out_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
-  return dtype == DT_BF16 ? out_proj_tc_launch<__nv_bfloat16>(a, st) : out_proj_tc_launch<__half>(a, st);
+  if (a.ln_out)
+    return dtype == DT_BF16 ? out_proj_tc_launch<__nv_bfloat16, true>(a, st) : out_proj_tc_launch<__half, true>(a, st);
+  return dtype == DT_BF16 ? out_proj_tc_launch<__nv_bfloat16, false>(a, st) : out_proj_tc_launch<__half, false>(a, st);
 }
 
 }  // namespace triattn

@@ -134,6 +134,11 @@ struct LayerArgs {
   Workspace wl;
   int* status;                 // device status word
   int num_sms;                 // multiprocessors of the current device (persistent grids)
+  // optional (16-bit path): this layer's LayerNorm output given by the caller (LN skipped; view in
+  // 16-bit elements), and the next module's LayerNorm applied to the output, written in 16 bits
+  const void* xn; View xnv;
+  const float* ln_next_w; const float* ln_next_b;
+  void* ln_out; View lnv;
 };
 
 // launchers (return cudaGetLastError())

@@ -135,12 +135,72 @@ class TriangleAttention(nn.Module):
                 use_kernels: bool = False, xn: Optional[torch.Tensor] = None, keep_t: bool = False) -> torch.Tensor:
         """x [B, I, J, c_in] -> update y [B, I, J, c_in] (same orientation as x).
 
-        `chunk_size` / `use_kernels` are accepted and ignored, as in the reference.  `xn` / `keep_t`
-        belong to the reference's fused f16 pair block (attention.py:95-103); this build reads z in
-        place in both orientations, so it takes neither."""
-        if xn is not None or keep_t:
-            raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED, "xn / keep_t (reference f16 pair-block plumbing)")
-        return self._run(x, mask, False, None)
+        `chunk_size` / `use_kernels` are accepted and ignored, as in the reference.  As in the reference's
+        f16 path (attention.py:95-103): `xn` = this module's LayerNorm output already computed (16-bit, the
+        module's type; for the ending node already transposed), so the LayerNorm is skipped; `keep_t` =
+        return the ending node's update in the transposed layout."""
+        if xn is None and not keep_t:
+            return self._run(x, mask, False, None)
+        return self._run_fused(x, mask, xn, add_residual=False, keep_t=keep_t)[0]
+
+    def f16_addln(self, z: torch.Tensor, mask: Optional[torch.Tensor], xn: Optional[torch.Tensor], ln_next,
+                  trans_out: bool = False, tb: Optional[torch.Tensor] = None, w_tb: Optional[torch.Tensor] = None):
+        """(z + self(z), ln_next(z + self(z)) 16-bit [transposed with trans_out][, next tri bias]) as the
+        reference's f16_addln (attention.py:170-190, kernels_nax3.linear_addln): the layer from
+        xn = this module's LayerNorm output (ending node: already transposed), then the output projection,
+        the residual add and the next module's LayerNorm in the output kernel's epilogue.
+
+        `ln_next`: a LayerNorm module (weight, bias; eps 1e-5).  `tb` (this module's tri bias precomputed
+        by the producer of xn) is accepted and not needed: the projection kernel derives the tri bias
+        from xn itself.  `w_tb` [H, c_in]: also return the next module's tri bias LN_out . w_tb^T as
+        [B, H, Q, K] (the layout of the reference's tb), from the 16-bit LayerNorm output."""
+        del tb
+        z_new, ln_out = self._run_fused(z, mask, xn, add_residual=True, keep_t=False, ln_next=ln_next,
+                                        trans_out=trans_out)
+        if w_tb is None:
+            return z_new, ln_out
+        w = w_tb.to(device=ln_out.device, dtype=ln_out.dtype)
+        tb_next = (ln_out @ w.t()).permute(0, 3, 1, 2).contiguous()
+        return z_new, ln_out, tb_next
+
+    def _run_fused(self, x, mask, xn, *, add_residual: bool, keep_t: bool, ln_next=None, trans_out: bool = False):
+        self._check_geometry()
+        if not x.is_cuda:
+            raise RuntimeError("TriangleAttention (B200) needs CUDA tensors; there is no CPU path")
+        dtype = _lib.dtype_code(self.precision)
+        if dtype == _lib.F32:
+            raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED,
+                                          "xn / keep_t / f16_addln belong to the 16-bit path (precision fp16 or bf16)")
+        t16 = torch.bfloat16 if dtype == _lib.BF16 else torch.float16
+        z = x.contiguous() if x.dtype == torch.float32 else x.float().contiguous()
+        B, N = z.shape[0], z.shape[1]
+        if z.dim() != 4 or z.shape[2] != N or z.shape[3] != self.c_in:
+            raise ValueError(f"x must be [B, N, N, {self.c_in}], got {tuple(z.shape)}")
+        if xn is not None:
+            if tuple(xn.shape) != tuple(z.shape):
+                raise ValueError(f"xn must be {tuple(z.shape)}, got {tuple(xn.shape)}")
+            xn = xn.to(device=z.device, dtype=t16).contiguous()
+        m = None
+        if mask is not None:
+            if tuple(mask.shape) != (B, N, N):
+                raise ValueError(f"mask must be [B, N, N] = {(B, N, N)}, got {tuple(mask.shape)}")
+            m = mask.to(device=z.device, dtype=torch.float32).contiguous()
+        out = torch.empty_like(z)
+        ln_out, lw, lb = None, None, None
+        if ln_next is not None:
+            lw = ln_next.weight.detach().to(device=z.device, dtype=torch.float32).contiguous()
+            lb = ln_next.bias.detach().to(device=z.device, dtype=torch.float32).contiguous()
+            ln_out = torch.empty(z.shape, dtype=t16, device=z.device)
+        packed = self.packed_weights(dtype)
+        nbytes = _lib.workspace_bytes(B, N, N, dtype)
+        ws = self._ws.get(nbytes, z.device)
+        out_attn = int(keep_t and not self.starting)
+        _lib.check(_lib.lib().triattn_forward_fused(
+            z.data_ptr(), _lib.ptr(xn), _lib.ptr(m), packed.data_ptr(), B, N, int(self.starting), float(self.inf),
+            dtype, int(add_residual), out.data_ptr(), out_attn, _lib.ptr(lw), _lib.ptr(lb), _lib.ptr(ln_out),
+            int(trans_out), ws.data_ptr(), ws.numel(), _lib.stream_handle(z.device)))
+        self._fused_keepalive = (xn, m, lw, lb)  # inputs stay alive until the (asynchronous) launch has run
+        return out, ln_out
 
     def forward_residual(self, z: torch.Tensor, mask: Optional[torch.Tensor] = None, *,
                          inplace: bool = False) -> torch.Tensor:

@@ -119,6 +119,24 @@ TRIATTN_API int triattn_ln_proj(const float* z, const void* packed, int B, int N
 TRIATTN_API int triattn_core(int B, int N, int row_begin, int row_end, int dtype, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* Fused-neighbour form of triattn_forward <- TriangleAttention._f16 / f16_addln
+ *   (boltz_mlx/layers/triangular_attention/attention.py:95-103,170-190; kernels_nax3.linear_addln
+ *   kernels_nax3.py:69-198; pair block kernels.py:1526-1547), 16-bit dtypes only:
+ *   xn       : NULL -> LayerNorm of z as in triattn_forward; else this layer's LayerNorm output
+ *              [B][N][N][128] in the layer's 16-bit type, laid out in the layer's attention orientation
+ *              (for the ending node already transposed, as the reference passes it); z is then read
+ *              only for the residual.
+ *   out_attn_layout : 0 -> out in z's orientation; 1 -> in the layer's attention orientation (the
+ *              reference's keep_t for the ending node).
+ *   ln_out   : NULL, or [B][N][N][128] 16-bit <- LayerNorm(ln_next_w, ln_next_b, eps 1e-5) of every
+ *              output row (the next module's input), in z's orientation (ln_out_swapped = 0) or with
+ *              the two N axes swapped (1; the reference's trans_out). */
+TRIATTN_API int triattn_forward_fused(const float* z, const void* xn, const float* mask, const void* packed, int B,
+                                      int N, int starting, float inf, int dtype, int add_residual, float* out,
+                                      int out_attn_layout, const float* ln_next_w, const float* ln_next_b,
+                                      void* ln_out, int ln_out_swapped, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
 /* ---- strided-view stages (row-sharded / column-blocked pair tensors) ------------------------
  * The _v variants address an attention-oriented VIEW of a pair tensor instead of a dense [B][N][N]
  * one: element (b, a, c, ch) of the view lives at
