@@ -339,25 +339,27 @@ cudaError_t launch_mask_prep_tc(const LayerArgs& a, cudaStream_t st) {
 }
 
 // =================================================================================================
-// Flash core, persistent.  A work item = (batch b, head h, 128-query tile qt, group of RG attention
+// Flash core, persistent.  A work item = (batch b, head h, 128-query tile qt, pair of attention
 // rows); items are numbered with qt fastest (CTAs running at the same time read the same rows' K/V
-// tiles, which stay in L2) and CTA c takes items c, c + gridDim.x, ...  The tri-bias tile of
-// (h, qt, kt) is loaded once per key tile and shared by the RG rows of the item.
-//   16 warps = four softmax warpgroups; warpgroup j owns row j of the item (TMEM lanes = queries).
+// tiles, which stay in L2) and CTA c takes items c, c + gridDim.x, ...  Two CTAs share each SM
+// (2 x 92 KB shared memory, 2 x 256 TMEM columns, 2 x 256 threads at 128 registers): each has its
+// own tri-bias stage, so the two drift out of phase and one's MMA waits overlap the other's softmax
+// (one CTA of four rows keeps its rows in lockstep through the shared stage: 8 % slower).  The
+// tri-bias tile of (h, qt, kt) is loaded once per key tile and shared by the CTA's rows.
+//   8 warps = two softmax warpgroups; warpgroup j owns row j of the item (TMEM lanes = queries).
 //   Each row's leader thread issues that row's work itself: the bulk copies of its Q, K and V tiles
 //   (one slot each, refilled as soon as the MMA that read the slot has completed; after the row's
 //   last tile of an item they are refilled with the first active tile of the row's next item) and
-//   its MMAs (S = Q K^T, then O = P V).  The tri-bias stages form one ring over the CTA's whole
-//   sequence of (item, key tile) steps; a stage is refilled by whichever warp is the last of the 16
-//   to finish reading it (an arrival counter in shared memory).
-// TMEM (512 columns): row j owns columns [128 j, 128 j + 128): S (fp32, log2 units) -> x (after the
+//   its MMAs (S = Q K^T, then O = P V).  The tri-bias stage is refilled by whichever warp is the
+//   last of the CTA's 8 to finish reading it (an arrival counter in shared memory).
+// TMEM (256 columns): row j owns columns [128 j, 128 j + 128): S (fp32, log2 units) -> x (after the
 // biases) -> P (fp16 pairs in columns 0..63) and the P.V partial (columns 64..111: 32 channels + the
 // row sum from V's ones column).  O is accumulated in registers with a lazy rescale.
 // =================================================================================================
-constexpr int CG_RG = 4;
+constexpr int CG_RG = 2;            // rows per CTA; two CTAs share an SM
 constexpr int CG_SOFTMAX_WARPS = 4 * CG_RG;
 constexpr int CG_THREADS = CG_SOFTMAX_WARPS * 32;
-constexpr int CG_NB = 3;                           // tri-bias stages
+constexpr int CG_NB = 1;                           // tri-bias stages
 constexpr int CG_SQ = 0;                           // RG Q tiles, 8 KB each
 constexpr int CG_SB = CG_SQ + CG_RG * 8192;        // NB tri-bias stages, 32 KB each (fp16)
 constexpr int CG_SMB = CG_SB + CG_NB * 32768;      // NB stages x RG mask-bias slices of 512 B
@@ -472,7 +474,7 @@ __device__ __forceinline__ uint32_t exp2_pair_poly_f16(float x0, float x1, uint6
 __device__ __forceinline__ void wg_sync(int j) { asm volatile("bar.sync %0, 128;" ::"r"(j + 1) : "memory"); }
 
 template <typename T>
-__global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) {
+__global__ void __launch_bounds__(CG_THREADS, 2) core_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + CG_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + CG_BAR + B_COUNT * 8);
@@ -533,7 +535,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
   if (tid < CG_RG * 32)
     reinterpret_cast<uint32_t*>(scls)[tid] = class_word(blockIdx.x, tid / 32, tid % 32);
   fence_proxy_async_smem();
-  if (warp == 0) tmem_alloc(tslot, 512);
+  if (warp == 0) tmem_alloc(tslot, CG_RG * 128);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
     mbar_arrive_expect_tx(bar + B_VF + j, 8192);
     bulk_g2s(smem + CG_SV + j * 12288, args.ws + args.wl.off_v + tile * 8192, 8192, bar + B_VF + j);
   };
-  // this warp is done reading the tri-bias stage of step (ii, kt); the last of the 16 warps refills
+  // this warp is done reading the tri-bias stage of step (ii, kt); the last of the CTA's 8 warps refills
   // that stage with step + NB
   auto release_bias = [&](int ii, int kt) {
     __syncwarp();
@@ -817,7 +819,7 @@ __global__ void __launch_bounds__(CG_THREADS, 1) core_tc_kernel(LayerArgs args) 
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 512);
+  if (warp == 0) tmem_dealloc(tbase, CG_RG * 128);
 }
 
 template <typename T>
@@ -825,7 +827,7 @@ static cudaError_t core_tc_launch(const LayerArgs& a, cudaStream_t st) {
   cudaFuncSetAttribute(core_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, CG_SMEM);
   const int R = a.row_end - a.row_begin;
   const int n_items = a.wl.NT * ((R + CG_RG - 1) / CG_RG) * a.B * HEADS;
-  const int grid = n_items < a.num_sms ? n_items : a.num_sms;
+  const int grid = n_items < 2 * a.num_sms ? n_items : 2 * a.num_sms;  // two resident CTAs per SM
   core_tc_kernel<T><<<grid, CG_THREADS, CG_SMEM, st>>>(a);
   return cudaGetLastError();
 }
