@@ -14,6 +14,8 @@ from .triangle_attention import (  # noqa: F401
     pack_weights,
 )
 from . import _lib  # noqa: F401
+from .weights import load_module, load_pairformer_triatt, read_safetensors, write_safetensors  # noqa: F401
 
 __all__ = ["Attention", "TriangleAttention", "TriangleAttentionStartingNode", "TriangleAttentionEndingNode",
-           "load_params", "pack_weights"]
+           "load_params", "pack_weights", "read_safetensors", "write_safetensors", "load_module",
+           "load_pairformer_triatt"]
