@@ -837,20 +837,29 @@ cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 }
 
 // =================================================================================================
-// Output projection (+ residual).  CTA = 128 pairs; y[128 x 128] = (core o sigmoid(g))[128 x 128] * W_o^T.
-// 256 threads: thread (part, row) gates channels 64 part .. + 64 of one query row, then reads TMEM
-// lanes of that row's quadrant for output channels 64 part .. + 64; every global load of a thread
-// is issued before it waits (g before the bulk copy lands, the residual before the MMA ends).
+// Output projection (+ residual, optionally + the next module's LayerNorm).  CTA = 128 pairs (one
+// query tile of one attention row): y[128 x 128] = (core o sigmoid(g))[128 x 128] * W_o^T, 256 threads.
+//   gate: warp w updates rows 16w..16w+15 of the core image; one warp instruction covers 8 rows x 4
+//     chunks of 8 channels (lane = row % 8 + 8 * (chunk % 4)): g is read in 64-byte runs of 8 rows and
+//     the image in four conflict-free 128-byte runs.
+//   epilogue: the accumulator is staged through shared memory (fp32 rows at a stride of 132 floats:
+//     conflict-free both ways), then warp w streams rows 16w..16w+15 whole (lane = 4 channels): the
+//     residual loads, the output stores and the next LayerNorm's 16-bit rows are full 512 / 256-byte
+//     runs, and the LayerNorm statistics are warp reductions over one row.
 // =================================================================================================
 constexpr int OP_THREADS = 256;
-constexpr int OP_SMEM = 65536 + 64;
+constexpr int OP_STAGE_LD = C_IN + 4;                 // staged row stride (floats)
+constexpr int OP_SMEM_BODY = TILE * OP_STAGE_LD * 4;  // 67584 B: covers the two 32 KB operand images
+constexpr int OP_SMEM = OP_SMEM_BODY + 64;
+static_assert(OP_SMEM_BODY >= 65536, "staging buffer overlays the operand images");
 
 template <typename T, bool LN_NEXT>
-__global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs args) {
+__global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
   unsigned char* sW = smem + 32768;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 65536);
+  float* stage = reinterpret_cast<float*>(smem);  // after the MMA: [128][OP_STAGE_LD] fp32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OP_SMEM_BODY);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ct = blockIdx.x, al = blockIdx.y, a = args.row_begin + al, b = blockIdx.z;
@@ -871,22 +880,25 @@ __global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs ar
     bulk_g2s(sA, args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + ct) * 32768, 32768, bars + 0);
     bulk_g2s(sW, args.packed + PackedLayout::img_o, 32768, bars + 0);
   }
-  // gate: the fp16 core image row times sigmoid(g) of the same (b, row, query), rounded once to T,
-  // in place (the MMA then reads a T image)
+  // ---- gate: the fp16 core image times sigmoid(g) of the same (b, row, query), rounded once to T, in
+  //      place (the MMA then reads a T image); g loads in flight before the image lands ----
   {
-    const int row = tid & 127, part = tid >> 7;
-    const int q = min(ct * TILE + row, N - 1);
-    const uint4* g = reinterpret_cast<const uint4*>(args.ws + args.wl.off_g + (((size_t)b * R + al) * N + q) * C_IN * 2) +
-                     8 * part;
+    const int r8 = lane & 7, kq = lane >> 3;
+    const unsigned char* gb = args.ws + args.wl.off_g + ((size_t)b * R + al) * N * C_IN * 2;
     uint4 gv[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) gv[i] = __ldcs(g + i);
+    for (int it = 0; it < 8; ++it) {
+      const int r = 16 * warp + 8 * (it >> 2) + r8, k = 4 * (it & 3) + kq;
+      const int q = min(ct * TILE + r, N - 1);
+      gv[it] = __ldcs(reinterpret_cast<const uint4*>(gb + ((size_t)q * C_IN + 8 * k) * 2));
+    }
     mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint4* cp = reinterpret_cast<uint4*>(sA + img_off(row, 8 * (8 * part + i), HC));
+    for (int it = 0; it < 8; ++it) {
+      const int r = 16 * warp + 8 * (it >> 2) + r8, k = 4 * (it & 3) + kq;
+      uint4* cp = reinterpret_cast<uint4*>(sA + img_off(r, 8 * k, HC));
       const uint4 cv = *cp;
-      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
+      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[it].x, gv[it].y, gv[it].z, gv[it].w};
       uint32_t ow[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -910,103 +922,74 @@ __global__ void __launch_bounds__(OP_THREADS, 2) out_proj_tc_kernel(LayerArgs ar
     }
     umma_commit(bars + 1);
   }
-  // epilogue: warp w reads TMEM lanes 32 (w % 4).. (its rows), output channels 64 (w / 4) .. + 64
-  const int quad = warp & 3, part = warp >> 2;
-  const int c = ct * TILE + quad * 32 + lane;
-  const bool valid = c < N;
-  const long long ooff = b * args.ov.s_batch + (long long)(a - args.ov.row0) * args.ov.s_row + view_col(args.ov, c) +
-                         64 * part;
-  const long long zoff = b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row + view_col(args.zv, c) +
-                         64 * part;
-  // all 16 residual float4 of this thread in flight before the MMA wait (out may alias z, so every
-  // load is issued before the first store)
-  float4 zz[16];
+  // ---- epilogue.  Warp w streams rows 16w..16w+15 (lane: channels 4 lane..+3); the residual of its
+  //      first 8 rows is in flight during the CTA barrier that follows the staging (out may alias z:
+  //      a row's residual is always read before that row is written, and rows belong to one warp) ----
+  auto row_off = [&](const View& v, int r) -> long long {
+    return b * v.s_batch + (long long)(a - v.row0) * v.s_row + view_col(v, ct * TILE + r);
+  };
+  float4 zz[8];
+  auto load_z = [&](int h) {
 #pragma unroll
-  for (int d = 0; d < 16; ++d)
-    zz[d] = (valid && args.add_residual) ? __ldcs(reinterpret_cast<const float4*>(args.z + zoff) + d)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-  __syncwarp();
-  mbar_wait(bars + 1, 0, status, DEV_TIMEOUT_MMA);
-  __syncwarp();
-  tc_fence_after();
-  // y (+ residual) for 32 output channels of this thread's row: TMEM columns 64 part + 32 h2 ..
-  auto y_chunk = [&](int h2, float4 (&y)[8]) {
-    uint32_t acc[32];
-    tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
-    tmem_ld_wait();
-    tmem_regs_ready(acc);
-#pragma unroll
-    for (int d = 0; d < 8; ++d) {
-      const float4 zd = zz[8 * h2 + d];
-      y[d] = make_float4(__uint_as_float(acc[4 * d]) + zd.x, __uint_as_float(acc[4 * d + 1]) + zd.y,
-                         __uint_as_float(acc[4 * d + 2]) + zd.z, __uint_as_float(acc[4 * d + 3]) + zd.w);
+    for (int i = 0; i < 8; ++i) {
+      const int r = 16 * warp + 8 * h + i;
+      zz[i] = (args.add_residual && ct * TILE + r < N)
+                  ? __ldcs(reinterpret_cast<const float4*>(args.z + row_off(args.zv, r)) + lane)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
-#pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    float4 y[8];
-    y_chunk(h2, y);
-    if (valid) {
-#pragma unroll
-      for (int d = 0; d < 8; ++d) __stcs(reinterpret_cast<float4*>(args.out + ooff) + 8 * h2 + d, y[d]);
-    }
-  }
+  float4 lw = make_float4(0.f, 0.f, 0.f, 0.f), lb = lw;
   if constexpr (LN_NEXT) {
-    // the next module's LayerNorm of the output rows (reference linear_addln, kernels_nax3.py:69-198):
-    // two-pass fp32 statistics over the row's 128 channels, whose halves live in threads (quad, lane)
-    // of parts 0 and 1; partial sums meet in shared memory (the operand images are free by now)
-    float* red = reinterpret_cast<float*>(sA);  // [2 statistics][2 parts][128 rows]
-    const int row = quad * 32 + lane;
-    float s1 = 0.f;
+    lw = __ldg(reinterpret_cast<const float4*>(args.ln_next_w) + lane);
+    lb = __ldg(reinterpret_cast<const float4*>(args.ln_next_b) + lane);
+  }
+  mbar_wait(bars + 1, 0, status, DEV_TIMEOUT_MMA);  // MMA done: the operand images are free for staging
+  __syncwarp();
+  tc_fence_after();
+  {
+    // TMEM -> stage: warp (quad, part) holds rows 32 quad.. (its lanes), columns 64 part..
+    const int quad = warp & 3, part = warp >> 2;
+    float* srow = stage + (quad * 32 + lane) * OP_STAGE_LD + 64 * part;
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
-      float4 y[8];
-      y_chunk(h2, y);
+      uint32_t acc[32];
+      tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
+      tmem_ld_wait();
+      tmem_regs_ready(acc);
 #pragma unroll
-      for (int d = 0; d < 8; ++d) s1 += (y[d].x + y[d].y) + (y[d].z + y[d].w);
+      for (int d = 0; d < 32; d += 4)
+        *reinterpret_cast<float4*>(srow + 32 * h2 + d) =
+            make_float4(__uint_as_float(acc[d]), __uint_as_float(acc[d + 1]), __uint_as_float(acc[d + 2]),
+                        __uint_as_float(acc[d + 3]));
     }
-    red[part * TILE + row] = s1;
-    __syncthreads();
-    const float mean = (red[row] + red[TILE + row]) * (1.0f / C_IN);
-    float s2 = 0.f;
+  }
+  load_z(0);
+  tc_fence_before();
+  __syncthreads();
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    if (h == 1) load_z(1);
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      float4 y[8];
-      y_chunk(h2, y);
-#pragma unroll
-      for (int d = 0; d < 8; ++d) {
-        const float d0 = y[d].x - mean, d1 = y[d].y - mean, d2 = y[d].z - mean, d3 = y[d].w - mean;
-        s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
-      }
-    }
-    red[2 * TILE + part * TILE + row] = s2;
-    __syncthreads();
-    const float rstd = rsqrtf((red[2 * TILE + row] + red[3 * TILE + row]) * (1.0f / C_IN) + LN_EPS);
-    {
-      uint16_t* lo = reinterpret_cast<uint16_t*>(args.ln_out) + b * args.lnv.s_batch +
-                     (long long)(a - args.lnv.row0) * args.lnv.s_row + view_col(args.lnv, c) + 64 * part;
-      const float4* lw4 = reinterpret_cast<const float4*>(args.ln_next_w + 64 * part);
-      const float4* lb4 = reinterpret_cast<const float4*>(args.ln_next_b + 64 * part);
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        float4 y[8];
-        y_chunk(h2, y);  // warp-collective TMEM load: every lane, valid row or not
-        if (!valid) continue;
-#pragma unroll
-        for (int d = 0; d < 8; d += 2) {
-          const float4 w0 = __ldg(lw4 + 8 * h2 + d), w1 = __ldg(lw4 + 8 * h2 + d + 1);
-          const float4 c0 = __ldg(lb4 + 8 * h2 + d), c1 = __ldg(lb4 + 8 * h2 + d + 1);
-          uint4 pk;
-          pk.x = H16<T>::pack((y[d].x - mean) * rstd * w0.x + c0.x, (y[d].y - mean) * rstd * w0.y + c0.y);
-          pk.y = H16<T>::pack((y[d].z - mean) * rstd * w0.z + c0.z, (y[d].w - mean) * rstd * w0.w + c0.w);
-          pk.z = H16<T>::pack((y[d + 1].x - mean) * rstd * w1.x + c1.x, (y[d + 1].y - mean) * rstd * w1.y + c1.y);
-          pk.w = H16<T>::pack((y[d + 1].z - mean) * rstd * w1.z + c1.z, (y[d + 1].w - mean) * rstd * w1.w + c1.w);
-          *reinterpret_cast<uint4*>(lo + 32 * h2 + 4 * d) = pk;
-        }
+    for (int i = 0; i < 8; ++i) {
+      const int r = 16 * warp + 8 * h + i;
+      if (ct * TILE + r >= N) continue;  // warp-uniform
+      const float4 s = *reinterpret_cast<const float4*>(stage + r * OP_STAGE_LD + 4 * lane);
+      const float4 y = make_float4(s.x + zz[i].x, s.y + zz[i].y, s.z + zz[i].z, s.w + zz[i].w);
+      __stcs(reinterpret_cast<float4*>(args.out + row_off(args.ov, r)) + lane, y);
+      if constexpr (LN_NEXT) {
+        // the next module's LayerNorm of the new row (reference linear_addln, kernels_nax3.py:69-198):
+        // two-pass fp32 statistics, one rounding to the 16-bit type
+        const float mean = warp_sum32((y.x + y.y) + (y.z + y.w)) * (1.0f / C_IN);
+        const float d0 = y.x - mean, d1 = y.y - mean, d2 = y.z - mean, d3 = y.w - mean;
+        const float var = warp_sum32((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3)) * (1.0f / C_IN);
+        const float rstd = rsqrtf(var + LN_EPS);
+        uint2 pk;
+        pk.x = H16<T>::pack(d0 * rstd * lw.x + lb.x, d1 * rstd * lw.y + lb.y);
+        pk.y = H16<T>::pack(d2 * rstd * lw.z + lb.z, d3 * rstd * lw.w + lb.w);
+        *(reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(args.ln_out) + row_off(args.lnv, r)) + lane) = pk;
       }
     }
   }
-  tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tbase, 128);
 }
