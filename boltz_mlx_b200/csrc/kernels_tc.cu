@@ -50,16 +50,16 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr int LP_THREADS = 512;
 constexpr int LP_W_BYTES = NPROJ * C_IN * 2;  // 131072
 constexpr int LP_A_BYTES = TILE * C_IN * 2;   // 32768
-constexpr int LP_SMEM = LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4 + 64;
+constexpr int LP_SMEM = LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4 + 64;
 
 template <typename T, bool XN>
 __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sW = smem;
   unsigned char* sA = smem + LP_W_BYTES;
-  float* sBias = reinterpret_cast<float*>(smem + LP_W_BYTES + LP_A_BYTES);  // [2][4][128]
-  float* sGb = reinterpret_cast<float*>(smem + LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4);  // g bias [128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4);
+  float* sBias = reinterpret_cast<float*>(smem + LP_W_BYTES + 2 * LP_A_BYTES);  // [2][4][128]
+  float* sGb = reinterpret_cast<float*>(smem + LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4);  // g bias [128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
   uint64_t* bar_w = bars;
   uint64_t* bar_mma = bars + 1;  // [2]: q|k half, v|g half
@@ -124,15 +124,12 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
-  float4 xv[8];
-  int tile = blockIdx.x;
-  if (tile < ntiles) load_rows(tile, xv);
-
-  for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
-    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
-    const int a = args.row_begin + al, c0 = ct * TILE;
+  // ---- one tile in three steps: LayerNorm into image it & 1, MMA, epilogue.  The LayerNorm of tile
+  //      it + 1 runs while the MMA of tile it executes (two operand images, two tri-bias buffers);
+  //      one CTA barrier per tile then hands over both the new image and the freed TMEM ----
+  auto ln_tile = [&](int it, const float4 (&xv)[8]) {
     float* sB = sBias + (it & 1) * HEADS * TILE;
-
+    unsigned char* sAi = sA + (it & 1) * LP_A_BYTES;
     // ---- LayerNorm of this warp's 8 rows -> operand image + tri-bias values ----
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -155,7 +152,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
         pk.y = H16<T>::pack(n2, n3);
       }
       // swizzled image: one row's 256 bytes are two 128-byte runs (no bank conflicts)
-      *reinterpret_cast<uint2*>(sA + sw128_off(r, 4 * lane, LP_A_BYTES / 2)) = pk;
+      *reinterpret_cast<uint2*>(sAi + sw128_off(r, 4 * lane, LP_A_BYTES / 2)) = pk;
       // four head sums at once: exchange halves (xor 16: heads 0,1 | 2,3; xor 8: one head each), then
       // three more butterfly steps; lane 8 hh ends with head hh's total
       float p[HEADS];
@@ -172,13 +169,9 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
       k += __shfl_xor_sync(0xffffffffu, k, 1);
       if ((lane & 7) == 0) sB[(lane >> 3) * TILE + r] = k;
     }
-    // the next tile's rows: in flight during the MMA and the epilogue
-    if (tile + (int)gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();  // image + tri-bias values complete; previous epilogue done with TMEM
-    tc_fence_after();
-
+  };
+  auto issue_mma = [&](int it) {
+    unsigned char* sAi = sA + (it & 1) * LP_A_BYTES;
     // ---- MMA: two N=256 halves, one commit each ----
     if (tid == 0) {
       if (it == 0) mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
@@ -188,7 +181,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
       for (int nh = 0; nh < 2; ++nh) {
 #pragma unroll
         for (int ks = 0; ks < C_IN / 16; ++ks) {
-          const uint64_t ad = smem_desc_sw128(smem_u32(sA) + (ks / 4) * (LP_A_BYTES / 2) + (ks % 4) * 32);
+          const uint64_t ad = smem_desc_sw128(smem_u32(sAi) + (ks / 4) * (LP_A_BYTES / 2) + (ks % 4) * 32);
           const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * C_IN);
           umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
         }
@@ -196,6 +189,11 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
       }
     }
 
+  };
+  auto tri_bias = [&](int it, int tile) {
+    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+    const int a = args.row_begin + al, c0 = ct * TILE;
+    const float* sB = sBias + (it & 1) * HEADS * TILE;
     // ---- tri-bias rows of attention row a: fp16, log2 domain, 128 x 128 block layout [k/8][q][8];
     //      one 16-byte chunk = 8 consecutive keys of one head (padded keys 0) ----
     if (tid < HEADS * (TILE / 8)) {
@@ -212,6 +210,10 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
           make_uint4(w[0], w[1], w[2], w[3]);
     }
 
+  };
+  auto epilogue = [&](int it, int tile) {
+    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+    const int c0 = ct * TILE;
     // ---- epilogue: warp w reads lanes 32*(w%4).., output type w/4 (0 q, 1 k, 2 v, 3 g) ----
     const int quad = warp & 3, tt = warp >> 2;
     const int r = quad * 32 + lane, c = c0 + r;
@@ -271,9 +273,30 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
         }
       }
     }
-    // both MMA halves read the operand image, which the next LayerNorm overwrites
-    if (tt < 2) mbar_wait(bar_mma + 1, it & 1, status, DEV_TIMEOUT_MMA);
+  };
+  float4 xv[8];
+  int tile = blockIdx.x;
+  if (tile < ntiles) {
+    load_rows(tile, xv);
+    ln_tile(0, xv);
+    if (tile + (int)gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
+    fence_proxy_async_smem();
+    __syncthreads();
+    issue_mma(0);
+  }
+  for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
+    const int nxt = tile + gridDim.x;
+    if (nxt < ntiles) {
+      ln_tile(it + 1, xv);  // overlaps the MMA of this tile
+      if (nxt + (int)gridDim.x < ntiles) load_rows(nxt + gridDim.x, xv);  // in flight for a whole tile
+      fence_proxy_async_smem();
+    }
+    tri_bias(it, tile);
+    epilogue(it, tile);
     tc_fence_before();
+    __syncthreads();  // image it + 1 and its tri-bias sums complete; every epilogue done with TMEM
+    tc_fence_after();
+    if (nxt < ntiles) issue_mma(it + 1);
   }
   __syncthreads();
   tc_fence_after();
