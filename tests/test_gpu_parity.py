@@ -124,12 +124,12 @@ def test_row_chunked_stages_equal_full(precision):
         assert torch.equal(out, full)
 
 
-@pytest.mark.parametrize("cfg", [1, 2])
+@pytest.mark.parametrize("cfg", [1, 2, 4])
 def test_benchmark_configs_sampled_rows(cfg):
-    """Configs 1 (N=384 fp16) and 2 (N=1024 bf16) at full size: start + end pair vs the oracle on a
-    sample of attention rows (first, last, padded and interior rows)."""
+    """Configs 1 (N=384 fp16), 2 (N=1024 bf16) and 4 (N=2048 bf16) at full size: start + end pair vs
+    the oracle on a sample of attention rows (first, last, padded and interior rows)."""
     z, pm, p = make_inputs(cfg)
-    precision = {1: "fp16", 2: "bf16"}[cfg]
+    precision = {1: "fp16", 2: "bf16", 4: "bf16"}[cfg]
     N = z.shape[1]
     zc, mc = z.cuda(), pm.cuda()
     n_pad = int((pm[0, 0] == 0).sum())
