@@ -540,6 +540,9 @@ def main():
     ap.add_argument("--config", type=int, default=None)
     ap.add_argument("--precision", default=None)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU block exchange: peer stores from the output projection + cross-GPU barrier "
+                         "(default), or NCCL all-to-alls")
     ap.add_argument("--case", type=int, default=None,
                     help="profiling case: run one start+end pair at this N once (after one warm-up pair), "
                          "check the device status and exit; nothing is timed")

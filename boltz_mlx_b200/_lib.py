@@ -22,7 +22,10 @@ EXPORTED = [
     "triattn_pack_weights", "triattn_workspace_bytes", "triattn_forward", "triattn_mask_prep",
     "triattn_ln_proj", "triattn_core", "triattn_out_proj", "triattn_mask_prep_v", "triattn_ln_proj_v",
     "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb", "triattn_forward_fused",
+    "triattn_out_proj_vt", "triattn_peer_alloc", "triattn_peer_free", "triattn_ipc_handle", "triattn_ipc_open",
+    "triattn_ipc_close", "triattn_peer_barrier",
 ]
+IPC_HANDLE_BYTES = 64
 
 
 class TriAttnError(RuntimeError):
@@ -76,6 +79,14 @@ def lib() -> ctypes.CDLL:
         L.triattn_ln_proj_vb.argtypes = [_vp, _l, _l, _l, _i, _l, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_out_proj_vb.argtypes = [_vp, _l, _l, _l, _i, _l, _vp, _l, _l, _l, _i, _l, _vp, _i, _i, _i, _i, _i,
                                           _i, _vp, _sz, _vp]
+        L.triattn_out_proj_vt.argtypes = [_vp, _l, _l, _l, _i, _l, _vp, _l, _l, _l, _i, _vp, _vp, _i, _i, _i, _i, _i,
+                                          _i, _vp, _sz, _vp]
+        L.triattn_peer_alloc.argtypes = [_sz, ctypes.POINTER(_vp)]
+        L.triattn_peer_free.argtypes = [_vp]
+        L.triattn_ipc_handle.argtypes = [_vp, ctypes.c_char_p]
+        L.triattn_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
+        L.triattn_ipc_close.argtypes = [_vp]
+        L.triattn_peer_barrier.argtypes = [_vp, _i, _i, ctypes.c_uint32, _vp]
         for name in EXPORTED:
             if name not in ("triattn_version", "triattn_last_error_string", "triattn_packed_weights_bytes",
                             "triattn_workspace_bytes"):
@@ -116,7 +127,7 @@ def stream_handle(device: torch.device) -> int:
 
 def device_status(clear: bool = True) -> int:
     """The device status word (0 = ok; 101..103 = a bounded wait ran out, 104 bad index, 105 unaligned
-    shared memory).  Synchronises."""
+    shared memory, 106 a cross-GPU barrier missed a peer).  Synchronises."""
     v = ctypes.c_int(0)
     check(lib().triattn_device_status(ctypes.byref(v), int(clear)))
     return v.value

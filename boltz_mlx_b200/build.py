@@ -14,7 +14,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libtriattn.so"
-SOURCES = ["capi.cu", "kernels_f32.cu", "kernels_tc.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "kernels_f32.cu", "kernels_tc.cu", "noalloc.cu", "peer.cu"]
 HEADERS = ["sm100.cuh", "triattn_internal.cuh"]
 
 NVCC_FLAGS = [

@@ -112,6 +112,7 @@ View pair_view(int N, int starting, int channels) {
   v.row0 = 0;
   v.cblk = 0;
   v.s_cblk = 0;
+  v.tab = nullptr;
   return v;
 }
 
@@ -242,6 +243,7 @@ static View make_view(int64_t sb, int64_t sr, int64_t sc, int row0, int cblk = 0
   View v;
   v.s_batch = sb; v.s_row = sr; v.s_col = sc; v.row0 = row0;
   v.cblk = cblk; v.s_cblk = s_cblk;
+  v.tab = nullptr;
   return v;
 }
 
@@ -292,15 +294,17 @@ int triattn_out_proj_v(const float* z, int64_t zs_batch, int64_t zs_row, int64_t
                              row_begin, row_end, dtype, add_residual, workspace, workspace_bytes, stream);
 }
 
-int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, int z_col_block,
-                        int64_t zs_col_block, float* out, int64_t os_batch, int64_t os_row, int64_t os_col,
-                        int o_col_block, int64_t os_col_block, const void* packed, int B, int N, int row_begin,
-                        int row_end, int dtype, int add_residual, void* workspace, size_t workspace_bytes,
-                        void* stream) {
+static int out_proj_blocks(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, int z_col_block,
+                           int64_t zs_col_block, float* out, int64_t os_batch, int64_t os_row, int64_t os_col,
+                           int o_col_block, int64_t os_col_block, const int64_t* o_block_table, const void* packed,
+                           int B, int N, int row_begin, int row_end, int dtype, int add_residual, void* workspace,
+                           size_t workspace_bytes, void* stream, const char* what) {
   if (int r = check_dims(B, N, dtype)) return r;
   if (int r = check_rows(N, row_begin, row_end)) return r;
   if (int r = check_view("out", out, os_batch, os_row, os_col, true)) return r;
   if (int r = check_blocks("out", N, o_col_block, os_col_block)) return r;
+  if (o_block_table && (o_col_block <= 0 || !aligned(o_block_table, 8)))
+    return fail(TRIATTN_EINVAL, "out: a block table needs column blocks and 8-byte alignment");
   if (add_residual) {
     if (int r = check_view("z", z, zs_batch, zs_row, zs_col, true)) return r;
     if (int r = check_blocks("z", N, z_col_block, zs_col_block)) return r;
@@ -309,10 +313,88 @@ int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs_row, int64_
   LayerArgs a = make_args(B, N, 1, row_begin, row_end, 0.f, z, nullptr, out, add_residual, packed, workspace, dtype);
   a.zv = make_view(zs_batch, zs_row, zs_col, row_begin, z_col_block, zs_col_block);
   a.ov = make_view(os_batch, os_row, os_col, row_begin, o_col_block, os_col_block);
+  a.ov.tab = reinterpret_cast<const long long*>(o_block_table);
   if (int r = check_ws(workspace, workspace_bytes, a.wl)) return r;
-  if (!a.status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  if (!a.status) return fail(TRIATTN_EINVAL, "device status word unavailable");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return finish(dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st), "out_proj_v");
+  return finish(dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st), what);
+}
+
+int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, int z_col_block,
+                        int64_t zs_col_block, float* out, int64_t os_batch, int64_t os_row, int64_t os_col,
+                        int o_col_block, int64_t os_col_block, const void* packed, int B, int N, int row_begin,
+                        int row_end, int dtype, int add_residual, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  return out_proj_blocks(z, zs_batch, zs_row, zs_col, z_col_block, zs_col_block, out, os_batch, os_row, os_col,
+                         o_col_block, os_col_block, nullptr, packed, B, N, row_begin, row_end, dtype, add_residual,
+                         workspace, workspace_bytes, stream, "out_proj_v");
+}
+
+int triattn_out_proj_vt(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col, int z_col_block,
+                        int64_t zs_col_block, float* out, int64_t os_batch, int64_t os_row, int64_t os_col,
+                        int o_col_block, const int64_t* o_block_table, const void* packed, int B, int N,
+                        int row_begin, int row_end, int dtype, int add_residual, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!o_block_table) return fail(TRIATTN_EINVAL, "out: block table is NULL");
+  return out_proj_blocks(z, zs_batch, zs_row, zs_col, z_col_block, zs_col_block, out, os_batch, os_row, os_col,
+                         o_col_block, 0, o_block_table, packed, B, N, row_begin, row_end, dtype, add_residual,
+                         workspace, workspace_bytes, stream, "out_proj_vt");
+}
+
+// ---- peer-store exchange: IPC-shareable buffers and the cross-GPU barrier ----------------------
+int triattn_peer_alloc(size_t bytes, void** dev_ptr) {
+  if (!dev_ptr || bytes == 0) return fail(TRIATTN_EINVAL, "peer_alloc: NULL result pointer or zero size");
+  *dev_ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (peer buffer)");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaMemset (peer buffer)");
+  }
+  *dev_ptr = p;
+  return TRIATTN_OK;
+}
+
+int triattn_peer_free(void* dev_ptr) {
+  if (!dev_ptr) return TRIATTN_OK;
+  return finish(cudaFree(dev_ptr), "cudaFree (peer buffer)");
+}
+
+int triattn_ipc_handle(void* dev_ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == TRIATTN_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!dev_ptr || !handle) return fail(TRIATTN_EINVAL, "ipc_handle: NULL pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, dev_ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  return TRIATTN_OK;
+}
+
+int triattn_ipc_open(const void* handle, void** dev_ptr) {
+  if (!dev_ptr || !handle) return fail(TRIATTN_EINVAL, "ipc_open: NULL pointer");
+  *dev_ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return finish(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int triattn_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return TRIATTN_OK;
+  return finish(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+}
+
+int triattn_peer_barrier(const uint64_t* flag_ptrs, int rank, int world, uint32_t epoch, void* stream) {
+  if (!flag_ptrs || !aligned(flag_ptrs, 8)) return fail(TRIATTN_EINVAL, "peer_barrier: flag table NULL or unaligned");
+  if (world < 1 || world > 32 || rank < 0 || rank >= world)
+    return fail(TRIATTN_EINVAL, "peer_barrier: rank %d of %d (1..32 ranks)", rank, world);
+  int* status = device_status_ptr();
+  if (!status) return fail(TRIATTN_EINVAL, "device status word unavailable");
+  return finish(launch_peer_barrier(reinterpret_cast<const unsigned long long*>(flag_ptrs), rank, world, epoch, status,
+                                    static_cast<cudaStream_t>(stream)),
+                "peer_barrier");
 }
 
 int triattn_forward_fused(const float* z, const void* xn, const float* mask, const void* packed, int B, int N,

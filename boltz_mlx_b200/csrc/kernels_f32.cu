@@ -362,6 +362,9 @@ __global__ void __launch_bounds__(256) out_proj_f32_kernel(LayerArgs args) {
       *reinterpret_cast<float4*>(args.out + off) = r;
     }
   }
+  // peer stores (output blocks in other GPUs' memory): performed system-wide before the kernel ends,
+  // ahead of the cross-GPU barrier that publishes them
+  if (args.ov.tab) __threadfence_system();
 }
 
 cudaError_t launch_out_proj_f32(const LayerArgs& a, cudaStream_t st) {

@@ -1013,6 +1013,9 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
       }
     }
   }
+  // peer stores (output blocks in other GPUs' memory): performed system-wide before the kernel ends,
+  // ahead of the cross-GPU barrier that publishes them
+  if (args.ov.tab || args.lnv.tab) __threadfence_system();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tbase, 128);
 }

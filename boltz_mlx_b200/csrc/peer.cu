@@ -1,0 +1,57 @@
+// Cross-GPU barrier of the peer-store exchange (one process per GPU, memory shared through CUDA IPC).
+//
+// Each rank owns a flag block of `world` 32-bit slots in IPC-shared device memory.  A barrier with
+// epoch e: lane t (< world) publishes e into slot [rank] of rank t's block (a system-scope release
+// store over NVLink), then waits until slot [t] of its own block holds e or later (system-scope
+// acquire loads).  Epochs only grow, so a late signal from the previous barrier cannot satisfy this
+// one.  The wait is bounded: after TRIATTN_WAIT_NS (or as soon as the status word holds an error)
+// the lane records DEV_PEER_TIMEOUT and returns, so a rank that never arrives cannot hang this GPU.
+#include <cstdint>
+
+#include "sm100.cuh"
+#include "triattn_internal.cuh"
+
+namespace triattn {
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(32) peer_barrier_kernel(const unsigned long long* __restrict__ flag_ptrs, int rank,
+                                                          int world, unsigned epoch, int* status) {
+  const int t = threadIdx.x;
+  if (t >= world) return;
+  __threadfence_system();  // this GPU's earlier writes (previous kernels included) before the signal
+  st_release_sys(reinterpret_cast<unsigned*>(flag_ptrs[t]) + rank, epoch);
+  const unsigned* mine = reinterpret_cast<const unsigned*>(flag_ptrs[rank]) + t;
+  uint64_t t0 = 0;
+  for (uint32_t spin = 0;; ++spin) {
+    if (static_cast<int>(ld_acquire_sys(mine) - epoch) >= 0) break;
+    if ((spin & 63u) == 0u) {
+      if (*reinterpret_cast<volatile int*>(status) != 0) return;
+      const uint64_t now = global_timer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > TRIATTN_WAIT_NS) {
+        atomicCAS(status, 0, DEV_PEER_TIMEOUT);
+        return;
+      }
+    }
+    __nanosleep(200);
+  }
+  __threadfence_system();
+}
+
+cudaError_t launch_peer_barrier(const unsigned long long* flag_ptrs, int rank, int world, unsigned epoch,
+                                int* status, cudaStream_t st) {
+  peer_barrier_kernel<<<1, 32, 0, st>>>(flag_ptrs, rank, world, epoch, status);
+  return cudaGetLastError();
+}
+
+}  // namespace triattn

@@ -112,14 +112,20 @@ __host__ __device__ __forceinline__ uint32_t vimg_off(uint32_t key, uint32_t ch)
 // (starting node: s_row = N*ch, s_col = ch; ending node: s_row = ch, s_col = N*ch; a row-sharded
 // residual stream kept as [P][rows][cols of rank p][ch] blocks: s_row = cblk*ch, s_col = ch,
 // s_cblk = rows*cblk*ch).
+// With a block table (tab != nullptr, device memory, N / cblk entries) block q starts at tab[q]
+// elements from base instead of q * s_cblk: the blocks may then sit in other GPUs' memory mapped
+// into this process (the peer-store exchange of the row-sharded layer).
 struct View {
   long long s_batch, s_row, s_col;
   int row0;
   int cblk;
   long long s_cblk;
+  const long long* tab;
 };
-__host__ __device__ __forceinline__ long long view_col(const View& v, int c) {
-  return v.cblk ? (long long)(c / v.cblk) * v.s_cblk + (long long)(c % v.cblk) * v.s_col : (long long)c * v.s_col;
+__device__ __forceinline__ long long view_col(const View& v, int c) {
+  if (!v.cblk) return (long long)c * v.s_col;
+  const int q = c / v.cblk;
+  return (v.tab ? __ldg(v.tab + q) : (long long)q * v.s_cblk) + (long long)(c - q * v.cblk) * v.s_col;
 }
 
 struct LayerArgs {
@@ -153,6 +159,8 @@ cudaError_t launch_out_proj_f32(const LayerArgs& a, cudaStream_t st);
 cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 cudaError_t launch_out_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
+cudaError_t launch_peer_barrier(const unsigned long long* flag_ptrs, int rank, int world, unsigned epoch,
+                                int* status, cudaStream_t st);
 int* device_status_ptr();
 int record_error(int code, const char* what, const char* detail);
 

@@ -17,12 +17,23 @@ multi-GPU form distributes those row chunks:
   back, lands in the same layout.  So a start+end pair (pair_blocks) costs two all-to-alls and no
   transposing copy.  pair() wraps it for callers that hold row-layout shards [R][N][C].
 
-The exchange steps are plain torch.distributed collectives, so the host logic also runs on CPU
-ranks with the gloo backend (tests/test_distributed_cpu.py).
+Two exchanges move the blocks:
+
+* exchange="nccl": the steps above as torch.distributed collectives (all_to_all_single), so the
+  host logic also runs on CPU ranks with the gloo backend (tests/test_distributed_cpu.py).
+* exchange="peer": no all-to-all at all.  Every rank's column buffer zc [N][R][C] and row-block
+  buffer zb [P][R][R][C] live in one CUDA-IPC-shared allocation mapped on every rank.  The starting
+  node's output projection reads z from zb and stores each output block straight into the column
+  buffer of the rank that owns those columns (NVLink stores, overlapped with the projection); the
+  ending node reads zc and stores its output blocks straight into the owners' zb.  A cross-GPU
+  barrier (bounded flag waits, libtriattn's triattn_peer_barrier) after each output projection
+  orders the layers.  The per-block destinations are a device table of element offsets
+  (peer_block_tables); the arithmetic per row is the same, so both exchanges give identical bits.
 """
 
 from __future__ import annotations
 
+import ctypes
 import json
 import os
 from typing import Optional
@@ -96,11 +107,107 @@ def cols_to_blocks(zt: torch.Tensor, z_blk: torch.Tensor, group=None) -> None:
     dist.all_to_all_single(z_blk, zt.view(P, R, R, Cc), group=group)
 
 
+class _DeviceArray:
+    """A raw device allocation described by __cuda_array_interface__ (torch.as_tensor wraps it
+    without a copy; the wrapper keeps `owner` alive)."""
+
+    def __init__(self, ptr: int, shape, typestr: str, owner):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+        self._owner = owner
+
+
+class PeerSpace:
+    """One IPC-shared device buffer per rank (triattn_peer_alloc), mapped on every rank of the group:
+    ptrs[q] is rank q's buffer as seen from this process (ptrs[rank] = the own buffer)."""
+
+    def __init__(self, nbytes: int, device: torch.device, group=None):
+        L = _lib.lib()
+        self.group, self.device, self.nbytes = group, device, nbytes
+        self.P, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        own = ctypes.c_void_p()
+        _lib.check(L.triattn_peer_alloc(nbytes, ctypes.byref(own)))
+        self.own = own.value
+        h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        _lib.check(L.triattn_ipc_handle(self.own, h))
+        handles = [None] * self.P
+        dist.all_gather_object(handles, h.raw, group=group)
+        self.ptrs, self._opened = [], []
+        for q, hq in enumerate(handles):
+            if q == self.rank:
+                self.ptrs.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(L.triattn_ipc_open(ctypes.create_string_buffer(hq, _lib.IPC_HANDLE_BYTES), ctypes.byref(p)))
+            self.ptrs.append(p.value)
+            self._opened.append(p.value)
+
+    def tensor(self, offset: int, shape, dtype=torch.float32) -> torch.Tensor:
+        """A view of this rank's own buffer at byte `offset`."""
+        typestr = {torch.float32: "<f4", torch.int64: "<i8", torch.int32: "<i4"}[dtype]
+        n = 1
+        for d in shape:
+            n *= d
+        if offset < 0 or offset + n * torch.empty((), dtype=dtype).element_size() > self.nbytes:
+            raise ValueError(f"view [{offset}, +{shape}) outside the {self.nbytes}-byte peer buffer")
+        return torch.as_tensor(_DeviceArray(self.own + offset, shape, typestr, self), device=self.device)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then free the own one once every rank has unmapped it.  Call
+        after the GPU work that uses them has finished, on every rank."""
+        if self.own is None:
+            return
+        L = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            _lib.check(L.triattn_ipc_close(p))
+        self._opened = []
+        dist.barrier(group=self.group)
+        _lib.check(L.triattn_peer_free(self.own))
+        self.own = None
+
+
+def peer_layout(N: int, P: int) -> dict:
+    """Byte offsets inside every rank's shared buffer: zc [N][R][C] fp32 (the rank's column block),
+    zb [P][R][R][C] fp32 (the rank's rows in column blocks), flags [P] uint32 (barrier slots)."""
+    R = N // P
+    zc = N * R * C_IN * 4
+    return {"zc": 0, "zb": zc, "flags": 2 * zc, "total": 2 * zc + max(256, 4 * P)}
+
+
+def peer_block_tables(ptrs: list, rank: int, N: int, P: int) -> tuple[list, list, list]:
+    """Destination tables of the peer exchange, element offsets for triattn_out_proj_vt.
+
+    start: the starting node's output view (attention row a = row i of z, column c = j) has base =
+      this rank's zc, s_row = R*C, s_col = C, blocks of R columns; block q lands in rank q's zc at
+      [a][c % R] (zc_q + (a*R + c%R)*C), so tab[q] = (zc_q - zc_own)/4 + r0*R*C.
+    end: the ending node's output view (a = column j of z, c = row i) has base = this rank's zb,
+      s_row = C, s_col = R*C; block q lands in rank q's zb at [rank][c % R][a - r0], so
+      tab[q] = (zb_q - zb_own)/4 + rank*R*R*C.
+    flags: the address of every rank's barrier slots."""
+    R, r0 = N // P, rank * (N // P)
+    lay = peer_layout(N, P)
+
+    def el(delta: int) -> int:
+        if delta % 4:
+            raise ValueError("peer buffers must be 4-byte aligned relative to one another")
+        return delta // 4
+
+    start = [el(ptrs[q] + lay["zc"] - (ptrs[rank] + lay["zc"])) + r0 * R * C_IN for q in range(P)]
+    end = [el(ptrs[q] + lay["zb"] - (ptrs[rank] + lay["zb"])) + rank * R * R * C_IN for q in range(P)]
+    flags = [ptrs[q] + lay["flags"] for q in range(P)]
+    return start, end, flags
+
+
 class ShardedPair:
     """One start+end triangle-attention pair on a row-sharded pair tensor (B = 1)."""
 
-    def __init__(self, N: int, precision: str, device: torch.device, group=None, inf: float = 1e9):
-        self.N, self.inf, self.device, self.group = N, inf, device, group
+    def __init__(self, N: int, precision: str, device: torch.device, group=None, inf: float = 1e9,
+                 exchange: str = "nccl"):
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
+        self.N, self.inf, self.device, self.group, self.exchange = N, inf, device, group, exchange
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.r0, self.r1 = shard_rows(N, self.P, self.rank)
@@ -111,16 +218,45 @@ class ShardedPair:
                                           f"16-bit row sharding needs rows per rank ({self.R}) to be a multiple of 128")
         self.w = Workspace.make(1, N, self.R, self.dt)
         self.ws = torch.empty(self.w.total, dtype=torch.uint8, device=device)
-        self.send = torch.empty(self.P, self.R, self.R, C_IN, device=device)
-        self.recv = torch.empty_like(self.send)
-        self.recv2 = torch.empty_like(self.send)
         self.L = _lib.lib()
+        self.peer = None
+        if exchange == "peer":
+            lay = peer_layout(N, self.P)
+            self.peer = PeerSpace(lay["total"], device, group)
+            self.zc = self.peer.tensor(lay["zc"], (N, self.R, C_IN))
+            self.zb = self.peer.tensor(lay["zb"], (self.P, self.R, self.R, C_IN))
+            t_start, t_end, flags = peer_block_tables(self.peer.ptrs, self.rank, N, self.P)
+            self.tab_start = torch.tensor(t_start, dtype=torch.int64, device=device)
+            self.tab_end = torch.tensor(t_end, dtype=torch.int64, device=device)
+            self.flag_tab = torch.tensor(flags, dtype=torch.int64, device=device)
+            self.epoch = 0
+            self.send = self.zb
+        else:
+            self.send = torch.empty(self.P, self.R, self.R, C_IN, device=device)
+            self.recv = torch.empty_like(self.send)
+            self.recv2 = torch.empty_like(self.send)
+
+    def _need_nccl(self) -> None:
+        if self.exchange != "nccl":
+            raise RuntimeError("this entry point uses the all-to-all exchange; the peer exchange runs pair_blocks")
+
+    def close(self) -> None:
+        """Release the shared buffers of the peer exchange (every rank, after the GPU work)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def barrier(self) -> None:
+        """Cross-GPU barrier on the current stream (peer exchange)."""
+        self.epoch += 1
+        _lib.check(self.L.triattn_peer_barrier(self.flag_tab.data_ptr(), self.rank, self.P, self.epoch, self._st()))
 
     def _st(self):
         return _lib.stream_handle(self.device)
 
     def start(self, z_loc: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
         """z_loc [R, N, 128] (rows r0..r1 of z) += TriAttStart(z) for those rows, in place."""
+        self._need_nccl()
         L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
         ws, nb = self.ws.data_ptr(), self.ws.numel()
         mptr = None if mask is None else mask.data_ptr() + r0 * N * 4
@@ -135,6 +271,7 @@ class ShardedPair:
 
     def end(self, z_loc: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
         """z_loc [R, N, 128] += TriAttEnd(z) for rows r0..r1, via the column block of z."""
+        self._need_nccl()
         L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
         ws, nb = self.ws.data_ptr(), self.ws.numel()
         zt = rows_to_cols(z_loc, self.P, self.send, self.recv, self.group)  # [N, R, 128]
@@ -152,6 +289,7 @@ class ShardedPair:
 
     def start_blocks(self, z_blk: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
         """z_blk [P, R, R, 128] (my rows of z, column blocks) += TriAttStart(z) for those rows, in place."""
+        self._need_nccl()
         L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
         ws, nb = self.ws.data_ptr(), self.ws.numel()
         mptr = None if mask is None else mask.data_ptr() + r0 * N * 4
@@ -168,6 +306,7 @@ class ShardedPair:
     def end_blocks(self, z_blk: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
         """z_blk += TriAttEnd(z) for my rows: all-to-all to my column block, the layer on it in place,
         all-to-all straight back into z_blk."""
+        self._need_nccl()
         L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
         ws, nb = self.ws.data_ptr(), self.ws.numel()
         zt = blocks_to_cols(z_blk, self.recv, self.group)  # [N, R, 128]
@@ -182,8 +321,53 @@ class ShardedPair:
                                         packed.data_ptr(), 1, N, r0, r1, dt, 1, ws, nb, st))
         cols_to_blocks(zt, z_blk, self.group)
 
+    def start_peer(self, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
+        """Starting node on zb (my rows, column blocks); the output z + y goes straight into the column
+        buffers zc of the owning ranks, then a barrier."""
+        L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
+        ws, nb = self.ws.data_ptr(), self.ws.numel()
+        mptr = None if mask is None else mask.data_ptr() + r0 * N * 4
+        _lib.check(L.triattn_mask_prep_v(mptr, N * N, N, 1, 1, N, self.inf, r0, r1, dt, ws, nb, st))
+        zp = self.zb.data_ptr()
+        s_row, s_col, cb, s_cb = R * C_IN, C_IN, R, R * R * C_IN
+        _lib.check(L.triattn_ln_proj_vb(zp, N * N * C_IN, s_row, s_col, cb, s_cb, packed.data_ptr(), 1, N, r0, r1, dt,
+                                        ws, nb, st))
+        gather_bias(self.ws, self.w, r0, r1, self.group)
+        _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
+        _lib.check(L.triattn_out_proj_vt(zp, N * N * C_IN, s_row, s_col, cb, s_cb, self.zc.data_ptr(), N * R * C_IN,
+                                         R * C_IN, C_IN, R, self.tab_start.data_ptr(), packed.data_ptr(), 1, N, r0,
+                                         r1, dt, 1, ws, nb, st))
+        self.barrier()
+
+    def end_peer(self, mask: Optional[torch.Tensor], packed: torch.Tensor) -> None:
+        """Ending node on zc (my columns); the output goes straight back into the row owners' zb,
+        then a barrier."""
+        L, N, R, r0, r1, dt, st = self.L, self.N, self.R, self.r0, self.r1, self.dt, self._st()
+        ws, nb = self.ws.data_ptr(), self.ws.numel()
+        mptr = None if mask is None else mask.data_ptr() + r0 * 4
+        _lib.check(L.triattn_mask_prep_v(mptr, N * N, 1, N, 1, N, self.inf, r0, r1, dt, ws, nb, st))
+        zp = self.zc.data_ptr()
+        _lib.check(L.triattn_ln_proj_v(zp, N * R * C_IN, C_IN, R * C_IN, packed.data_ptr(), 1, N, r0, r1, dt, ws, nb,
+                                       st))
+        gather_bias(self.ws, self.w, r0, r1, self.group)
+        _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
+        _lib.check(L.triattn_out_proj_vt(zp, N * R * C_IN, C_IN, R * C_IN, 0, 0, self.zb.data_ptr(), N * N * C_IN,
+                                         C_IN, R * C_IN, R, self.tab_end.data_ptr(), packed.data_ptr(), 1, N, r0, r1,
+                                         dt, 1, ws, nb, st))
+        self.barrier()
+
     def pair_blocks(self, z_blk, mask, packed_start, packed_end) -> None:
-        """One start+end pair on the block-layout residual stream (two all-to-alls, no copies)."""
+        """One start+end pair on the block-layout residual stream.  nccl: two all-to-alls, no copies.
+        peer: z_blk should be self.zb (the shared buffer; anything else is copied in and out)."""
+        if self.exchange == "peer":
+            own = z_blk.data_ptr() == self.zb.data_ptr()
+            if not own:
+                self.zb.copy_(z_blk)
+            self.start_peer(mask, packed_start)
+            self.end_peer(mask, packed_end)
+            if not own:
+                z_blk.copy_(self.zb)
+            return
         self.start_blocks(z_blk, mask, packed_start)
         self.end_blocks(z_blk, mask, packed_end)
 
@@ -195,7 +379,8 @@ class ShardedPair:
 
     def nvlink_bytes_per_pair(self) -> int:
         """Bytes each rank sends over NVLink per pair: 2 tri-bias all-gathers (its own bias rows to each
-        of the P - 1 peers) + 2 all-to-alls of fp32 z blocks."""
+        of the P - 1 peers) + 2 exchanges of fp32 z blocks (all-to-alls, or the same bytes as peer
+        stores)."""
         b0, b1 = self.w.bias_rows(self.r0, self.r1)
         bias = (self.P - 1) * (b1 - b0)
         a2a = (self.P - 1) * self.R * self.R * C_IN * 4
@@ -219,7 +404,8 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         z_h, pm_h, ps, pe = make_config_inputs(args.config)
         N = z_h.shape[1]
         prec = args.precision or {0: "fp32", 1: "fp16"}.get(args.config, "bf16")
-        sp = ShardedPair(N, prec, dev)
+        exchange = getattr(args, "exchange", "peer")
+        sp = ShardedPair(N, prec, dev, exchange=exchange)
         packs = []
         for starting, p in ((True, ps), (False, pe)):
             m = TriangleAttention(starting=starting, precision=prec).to(dev)
@@ -228,7 +414,7 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         mask = pm_h[0].contiguous().to(dev)
         z_loc = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
         # the residual stream stays in block layout across steps (the layout the exchange uses)
-        z_blk = to_blocks(z_loc, sp.P, torch.empty(sp.P, sp.R, sp.R, C_IN, device=dev))
+        z_blk = to_blocks(z_loc, sp.P, sp.zb if exchange == "peer" else torch.empty(sp.P, sp.R, sp.R, C_IN, device=dev))
 
         def step():  # in place: every step is the same work on the updated shard
             sp.pair_blocks(z_blk, mask, packs[0], packs[1])
@@ -327,6 +513,8 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
                 "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
                 "config": workload_config(args.config, ws_n),
                 "nvlink_bytes_per_rank_per_step": sp.nvlink_bytes_per_pair(),
+                "exchange": {"peer": "peer stores from the output projection + cross-GPU barrier (CUDA IPC)",
+                             "nccl": "NCCL all_to_all_single"}[exchange],
                 "roofline": {"bound": "tensor", "kernel": "core_tc (flash attention core, this rank's rows)",
                              "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
                              "frac": achieved / tensor_peak, "peak_kind": f"{pk_kind} bf16 burst, per GPU",
@@ -336,11 +524,13 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
                         "ms_per_step": float(e2e), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
                         "d2h_bytes_per_step": oh.numel() * 4 * ws_n,
                         "pipelined": "input copy, pair and output copy of consecutive steps overlap (2 device slots)"},
-                "gpu_launches": args.steps * 2 * 4,
+                "gpu_launches": args.steps * 2 * (5 if exchange == "peer" else 4),
                 "device_status": int(status),
                 "clocks": clk.summary(),
             }
             print(json.dumps(line), flush=True)
     finally:
+        if "sp" in locals():
+            sp.close()
         dist.barrier()
         dist.destroy_process_group()

@@ -7,7 +7,8 @@
  *
  * Conventions
  *   - Every pointer argument is a DEVICE pointer unless stated otherwise; the caller allocates every
- *     output, the packed weights and the workspace.  The library never allocates or frees memory.
+ *     output, the packed weights and the workspace.  The library never allocates or frees memory
+ *     except in triattn_peer_alloc / triattn_peer_free (buffers shared between GPUs).
  *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream).  Calls are
  *     asynchronous: they validate arguments on the host, enqueue kernels and return.
  *   - Tensors are dense and row-major ("contiguous"): z/out [B][N][N][128] fp32, mask [B][N][N] fp32.
@@ -72,7 +73,7 @@ TRIATTN_API const char* triattn_last_error_string(void);
 
 /* Read the device status word of the current device (0 = ok; 101 a bulk copy, 102 an MMA, 103 a
  * barrier wait ran out; 104 an index check failed; 105 a shared-memory base was not aligned as a
- * swizzled operand needs); clear it when `clear` != 0.
+ * swizzled operand needs; 106 a cross-GPU barrier missed a peer); clear it when `clear` != 0.
  * Synchronises the device.  Returns TRIATTN_OK and writes the word to *status. */
 TRIATTN_API int triattn_device_status(int* status, int clear);
 
@@ -170,6 +171,40 @@ TRIATTN_API int triattn_out_proj_vb(const float* z, int64_t zs_batch, int64_t zs
                                     int64_t os_row, int64_t os_col, int o_col_block, int64_t os_col_block,
                                     const void* packed, int B, int N, int row_begin, int row_end, int dtype,
                                     int add_residual, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- peer-store exchange (one process per GPU of a node) -------------------------------------
+ * No reference counterpart: the reference runs on one device and bounds memory by row chunking
+ * (attention.py:55-68).  A row-sharded layer hands its output blocks to the ranks that consume them
+ * by storing them into those ranks' memory over NVLink from inside the output projection, instead of
+ * an all-to-all after it.  Shared buffers come from triattn_peer_alloc (a zero-filled allocation of
+ * their own, so an IPC handle maps exactly the buffer); the caller exchanges the 64-byte handles
+ * (an all-gather on its process group) and opens every other rank's with triattn_ipc_open.  Close
+ * the mappings on every rank before any owner frees its buffer. */
+#define TRIATTN_IPC_HANDLE_BYTES 64
+TRIATTN_API int triattn_peer_alloc(size_t bytes, void** dev_ptr);
+TRIATTN_API int triattn_peer_free(void* dev_ptr);
+TRIATTN_API int triattn_ipc_handle(void* dev_ptr, void* handle);
+TRIATTN_API int triattn_ipc_open(const void* handle, void** dev_ptr);
+TRIATTN_API int triattn_ipc_close(void* dev_ptr);
+
+/* Output projection (+ residual) whose column blocks lie anywhere in this process's address space
+ * (mapped peer buffers included): column c of the output view lives at
+ *     out + o_block_table[c / o_col_block] + (c % o_col_block)*os_col       (in elements)
+ * o_block_table is DEVICE memory, N / o_col_block int64 entries (element offsets from out; peer
+ * mappings give offsets outside out's own allocation).  The z view is as in triattn_out_proj_vb.
+ * Every store is made visible system-wide before the kernel ends; a triattn_peer_barrier after it on
+ * the same stream publishes the blocks to their owners. */
+TRIATTN_API int triattn_out_proj_vt(const float* z, int64_t zs_batch, int64_t zs_row, int64_t zs_col,
+                                    int z_col_block, int64_t zs_col_block, float* out, int64_t os_batch,
+                                    int64_t os_row, int64_t os_col, int o_col_block, const int64_t* o_block_table,
+                                    const void* packed, int B, int N, int row_begin, int row_end, int dtype,
+                                    int add_residual, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Cross-GPU barrier on `stream`.  flag_ptrs: DEVICE array of `world` uint64 addresses, entry t = rank
+ * t's flag block (world 32-bit slots, zero-filled at start) as mapped in this process.  Every rank
+ * calls it with the same epoch sequence (1, 2, 3, ...).  Bounded: a peer that does not arrive within
+ * 2 s leaves device status 106 (triattn_device_status) and the kernel returns. */
+TRIATTN_API int triattn_peer_barrier(const uint64_t* flag_ptrs, int rank, int world, uint32_t epoch, void* stream);
 
 /* Output projection (+ residual) of rows [row_begin,row_end), written in z's orientation. */
 TRIATTN_API int triattn_out_proj(const float* z, const void* packed, int B, int N, int starting, int row_begin, int row_end,
