@@ -23,7 +23,7 @@ EXPORTED = [
     "triattn_ln_proj", "triattn_core", "triattn_out_proj", "triattn_mask_prep_v", "triattn_ln_proj_v",
     "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb", "triattn_forward_fused",
     "triattn_out_proj_vt", "triattn_peer_alloc", "triattn_peer_free", "triattn_ipc_handle", "triattn_ipc_open",
-    "triattn_ipc_close", "triattn_peer_barrier",
+    "triattn_ipc_close", "triattn_peer_barrier", "triattn_peer_broadcast",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         L.triattn_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
         L.triattn_ipc_close.argtypes = [_vp]
         L.triattn_peer_barrier.argtypes = [_vp, _i, _i, ctypes.c_uint32, _vp]
+        L.triattn_peer_broadcast.argtypes = [_vp, _i, _i, _sz, _sz, _vp]
         for name in EXPORTED:
             if name not in ("triattn_version", "triattn_last_error_string", "triattn_packed_weights_bytes",
                             "triattn_workspace_bytes"):

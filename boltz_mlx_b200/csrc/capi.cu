@@ -386,6 +386,17 @@ int triattn_ipc_close(void* dev_ptr) {
   return finish(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
 }
 
+int triattn_peer_broadcast(const uint64_t* buf_ptrs, int rank, int world, size_t offset, size_t bytes,
+                           void* stream) {
+  if (!buf_ptrs || !aligned(buf_ptrs, 8)) return fail(TRIATTN_EINVAL, "peer_broadcast: pointer table NULL or unaligned");
+  if (world < 1 || world > 32 || rank < 0 || rank >= world)
+    return fail(TRIATTN_EINVAL, "peer_broadcast: rank %d of %d (1..32 ranks)", rank, world);
+  if (offset % 16 || bytes % 16) return fail(TRIATTN_EINVAL, "peer_broadcast: offset and size must be multiples of 16");
+  return finish(launch_peer_broadcast(reinterpret_cast<const unsigned long long*>(buf_ptrs), rank, world, offset, bytes,
+                                      device_sm_count(), static_cast<cudaStream_t>(stream)),
+                "peer_broadcast");
+}
+
 int triattn_peer_barrier(const uint64_t* flag_ptrs, int rank, int world, uint32_t epoch, void* stream) {
   if (!flag_ptrs || !aligned(flag_ptrs, 8)) return fail(TRIATTN_EINVAL, "peer_barrier: flag table NULL or unaligned");
   if (world < 1 || world > 32 || rank < 0 || rank >= world)

@@ -6,6 +6,7 @@
 // acquire loads).  Epochs only grow, so a late signal from the previous barrier cannot satisfy this
 // one.  The wait is bounded: after TRIATTN_WAIT_NS (or as soon as the status word holds an error)
 // the lane records DEV_PEER_TIMEOUT and returns, so a rank that never arrives cannot hang this GPU.
+#include <algorithm>
 #include <cstdint>
 
 #include "sm100.cuh"
@@ -51,6 +52,41 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const unsigned long lo
 cudaError_t launch_peer_barrier(const unsigned long long* flag_ptrs, int rank, int world, unsigned epoch,
                                 int* status, cudaStream_t st) {
   peer_barrier_kernel<<<1, 32, 0, st>>>(flag_ptrs, rank, world, epoch, status);
+  return cudaGetLastError();
+}
+
+}  // namespace triattn
+
+namespace triattn {
+
+// Copy `bytes` (a multiple of 16) at byte `offset` of this rank's buffer to the same offset of every
+// other rank's buffer (dst_ptrs[t] = rank t's buffer as mapped here): 16-byte loads from local HBM,
+// stores over NVLink, all peers interleaved so every link carries traffic at once.  The stores are
+// made visible system-wide before the kernel ends (a triattn_peer_barrier publishes them).
+__global__ void __launch_bounds__(256) peer_broadcast_kernel(const unsigned long long* __restrict__ dst_ptrs,
+                                                             int rank, int world, size_t offset, size_t n16) {
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(dst_ptrs[rank]) + offset);
+  const int lane = threadIdx.x & 31;
+  const size_t peers = (size_t)(world - 1);
+  // work unit = 32 consecutive 16-byte chunks (512 B) for one peer; units cycle over the peers
+  const size_t units = (n16 + 31) / 32 * peers;
+  const size_t nwarps = (size_t)gridDim.x * (blockDim.x >> 5);
+  for (size_t u = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+    const size_t g = u / peers;
+    int t = (int)(u - g * peers);
+    t += (t >= rank);
+    const size_t k = g * 32 + lane;
+    if (k < n16) reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst_ptrs[t]) + offset)[k] = __ldg(src + k);
+  }
+  __threadfence_system();
+}
+
+cudaError_t launch_peer_broadcast(const unsigned long long* dst_ptrs, int rank, int world, size_t offset, size_t bytes,
+                                  int num_sms, cudaStream_t st) {
+  if (world < 2 || bytes == 0) return cudaSuccess;
+  const size_t n16 = bytes / 16, units = (n16 + 31) / 32 * (size_t)(world - 1);
+  const int grid = (int)std::max<size_t>(1, std::min<size_t>((size_t)num_sms * 4, (units + 7) / 8));
+  peer_broadcast_kernel<<<grid, 256, 0, st>>>(dst_ptrs, rank, world, offset, n16);
   return cudaGetLastError();
 }
 

@@ -161,6 +161,8 @@ cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 cudaError_t launch_out_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st);
 cudaError_t launch_peer_barrier(const unsigned long long* flag_ptrs, int rank, int world, unsigned epoch,
                                 int* status, cudaStream_t st);
+cudaError_t launch_peer_broadcast(const unsigned long long* dst_ptrs, int rank, int world, size_t offset, size_t bytes,
+                                  int num_sms, cudaStream_t st);
 int* device_status_ptr();
 int record_error(int code, const char* what, const char* detail);
 

@@ -28,7 +28,10 @@ Two exchanges move the blocks:
   ending node reads zc and stores its output blocks straight into the owners' zb.  A cross-GPU
   barrier (bounded flag waits, libtriattn's triattn_peer_barrier) after each output projection
   orders the layers.  The per-block destinations are a device table of element offsets
-  (peer_block_tables); the arithmetic per row is the same, so both exchanges give identical bits.
+  (peer_block_tables).  The workspaces live in the shared allocation too: each rank stores its
+  tri-bias rows into every other rank's bias region with one broadcast launch
+  (triattn_peer_broadcast) and a barrier, in place of the all-gather.  The arithmetic per row is
+  the same, so both exchanges give identical bits.
 """
 
 from __future__ import annotations
@@ -144,7 +147,7 @@ class PeerSpace:
 
     def tensor(self, offset: int, shape, dtype=torch.float32) -> torch.Tensor:
         """A view of this rank's own buffer at byte `offset`."""
-        typestr = {torch.float32: "<f4", torch.int64: "<i8", torch.int32: "<i4"}[dtype]
+        typestr = {torch.float32: "<f4", torch.int64: "<i8", torch.int32: "<i4", torch.uint8: "|u1"}[dtype]
         n = 1
         for d in shape:
             n *= d
@@ -168,12 +171,14 @@ class PeerSpace:
         self.own = None
 
 
-def peer_layout(N: int, P: int) -> dict:
+def peer_layout(N: int, P: int, ws_bytes: int = 0) -> dict:
     """Byte offsets inside every rank's shared buffer: zc [N][R][C] fp32 (the rank's column block),
-    zb [P][R][R][C] fp32 (the rank's rows in column blocks), flags [P] uint32 (barrier slots)."""
+    zb [P][R][R][C] fp32 (the rank's rows in column blocks), flags [P] uint32 (barrier slots), ws
+    (the rank's libtriattn workspace: peers store their tri-bias rows into its bias region)."""
     R = N // P
     zc = N * R * C_IN * 4
-    return {"zc": 0, "zb": zc, "flags": 2 * zc, "total": 2 * zc + max(256, 4 * P)}
+    ws = 2 * zc + (4 * P + 255) // 256 * 256
+    return {"zc": 0, "zb": zc, "flags": 2 * zc, "ws": ws, "total": ws + ws_bytes}
 
 
 def peer_block_tables(ptrs: list, rank: int, N: int, P: int) -> tuple[list, list, list]:
@@ -217,21 +222,23 @@ class ShardedPair:
             raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED,
                                           f"16-bit row sharding needs rows per rank ({self.R}) to be a multiple of 128")
         self.w = Workspace.make(1, N, self.R, self.dt)
-        self.ws = torch.empty(self.w.total, dtype=torch.uint8, device=device)
         self.L = _lib.lib()
         self.peer = None
         if exchange == "peer":
-            lay = peer_layout(N, self.P)
+            self.lay = lay = peer_layout(N, self.P, self.w.total)
             self.peer = PeerSpace(lay["total"], device, group)
             self.zc = self.peer.tensor(lay["zc"], (N, self.R, C_IN))
             self.zb = self.peer.tensor(lay["zb"], (self.P, self.R, self.R, C_IN))
+            self.ws = self.peer.tensor(lay["ws"], (self.w.total,), torch.uint8)
             t_start, t_end, flags = peer_block_tables(self.peer.ptrs, self.rank, N, self.P)
             self.tab_start = torch.tensor(t_start, dtype=torch.int64, device=device)
             self.tab_end = torch.tensor(t_end, dtype=torch.int64, device=device)
             self.flag_tab = torch.tensor(flags, dtype=torch.int64, device=device)
+            self.buf_tab = torch.tensor(self.peer.ptrs, dtype=torch.int64, device=device)
             self.epoch = 0
             self.send = self.zb
         else:
+            self.ws = torch.empty(self.w.total, dtype=torch.uint8, device=device)
             self.send = torch.empty(self.P, self.R, self.R, C_IN, device=device)
             self.recv = torch.empty_like(self.send)
             self.recv2 = torch.empty_like(self.send)
@@ -250,6 +257,14 @@ class ShardedPair:
         """Cross-GPU barrier on the current stream (peer exchange)."""
         self.epoch += 1
         _lib.check(self.L.triattn_peer_barrier(self.flag_tab.data_ptr(), self.rank, self.P, self.epoch, self._st()))
+
+    def share_bias(self) -> None:
+        """Peer exchange: store this rank's tri-bias rows into every other rank's workspace (one
+        launch over NVLink), then a barrier: the all-gather of the NCCL exchange."""
+        b0, b1 = self.w.bias_rows(self.r0, self.r1)
+        _lib.check(self.L.triattn_peer_broadcast(self.buf_tab.data_ptr(), self.rank, self.P, self.lay["ws"] + b0,
+                                                 b1 - b0, self._st()))
+        self.barrier()
 
     def _st(self):
         return _lib.stream_handle(self.device)
@@ -332,7 +347,7 @@ class ShardedPair:
         s_row, s_col, cb, s_cb = R * C_IN, C_IN, R, R * R * C_IN
         _lib.check(L.triattn_ln_proj_vb(zp, N * N * C_IN, s_row, s_col, cb, s_cb, packed.data_ptr(), 1, N, r0, r1, dt,
                                         ws, nb, st))
-        gather_bias(self.ws, self.w, r0, r1, self.group)
+        self.share_bias()
         _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
         _lib.check(L.triattn_out_proj_vt(zp, N * N * C_IN, s_row, s_col, cb, s_cb, self.zc.data_ptr(), N * R * C_IN,
                                          R * C_IN, C_IN, R, self.tab_start.data_ptr(), packed.data_ptr(), 1, N, r0,
@@ -349,7 +364,7 @@ class ShardedPair:
         zp = self.zc.data_ptr()
         _lib.check(L.triattn_ln_proj_v(zp, N * R * C_IN, C_IN, R * C_IN, packed.data_ptr(), 1, N, r0, r1, dt, ws, nb,
                                        st))
-        gather_bias(self.ws, self.w, r0, r1, self.group)
+        self.share_bias()
         _lib.check(L.triattn_core(1, N, r0, r1, dt, ws, nb, st))
         _lib.check(L.triattn_out_proj_vt(zp, N * R * C_IN, C_IN, R * C_IN, 0, 0, self.zb.data_ptr(), N * N * C_IN,
                                          C_IN, R * C_IN, R, self.tab_end.data_ptr(), packed.data_ptr(), 1, N, r0, r1,

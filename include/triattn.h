@@ -200,6 +200,13 @@ TRIATTN_API int triattn_out_proj_vt(const float* z, int64_t zs_batch, int64_t zs
                                     const void* packed, int B, int N, int row_begin, int row_end, int dtype,
                                     int add_residual, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Copy bytes [offset, offset + bytes) of this rank's shared buffer to the same range of every other
+ * rank's (buf_ptrs: DEVICE array of `world` uint64 buffer addresses as mapped here; offset and bytes
+ * multiples of 16).  One launch, all peers' links at once; the row-sharded layer hands its tri-bias
+ * rows to every rank this way.  Publish with triattn_peer_barrier. */
+TRIATTN_API int triattn_peer_broadcast(const uint64_t* buf_ptrs, int rank, int world, size_t offset, size_t bytes,
+                                       void* stream);
+
 /* Cross-GPU barrier on `stream`.  flag_ptrs: DEVICE array of `world` uint64 addresses, entry t = rank
  * t's flag block (world 32-bit slots, zero-filled at start) as mapped in this process.  Every rank
  * calls it with the same epoch sequence (1, 2, 3, ...).  Bounded: a peer that does not arrive within

@@ -113,3 +113,9 @@ def test_peer_barrier_times_out_without_a_peer():
     assert _lib.device_status() == 0
     x = torch.ones(1024, device=dev)
     assert float(x.sum()) == 1024.0
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_sharded_pair_four_ranks(exchange):
+    _run(4, 512, "bf16", exchange, steps=2)

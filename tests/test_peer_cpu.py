@@ -68,8 +68,9 @@ def test_peer_layout_keeps_regions_apart():
         R = N // P
         assert lay["zb"] - lay["zc"] == N * R * C * 4
         assert lay["flags"] - lay["zb"] == P * R * R * C * 4
-        assert lay["total"] - lay["flags"] >= 4 * P
-        assert lay["zb"] % 256 == 0 and lay["flags"] % 256 == 0
+        assert lay["ws"] - lay["flags"] >= 4 * P
+        assert lay["zb"] % 256 == 0 and lay["flags"] % 256 == 0 and lay["ws"] % 256 == 0
+        assert peer_layout(N, P, ws_bytes=1000)["total"] == lay["ws"] + 1000
 
 
 def test_peer_tables_reject_misaligned_buffers():
@@ -93,6 +94,11 @@ def test_peer_entry_points_validate_on_the_host():
     assert L.triattn_peer_barrier(4096 + 4, 0, 2, 1, None) == _lib.EINVAL
     assert L.triattn_peer_barrier(4096, 2, 2, 1, None) == _lib.EINVAL
     assert L.triattn_peer_barrier(4096, 0, 33, 1, None) == _lib.EINVAL
+    # broadcast: table, rank and 16-byte granularity checked before any launch
+    assert L.triattn_peer_broadcast(None, 0, 2, 0, 256, None) == _lib.EINVAL
+    assert L.triattn_peer_broadcast(4096, 3, 2, 0, 256, None) == _lib.EINVAL
+    assert L.triattn_peer_broadcast(4096, 0, 2, 8, 256, None) == _lib.EINVAL
+    assert L.triattn_peer_broadcast(4096, 0, 2, 0, 250, None) == _lib.EINVAL
     # block-table output projection: the table is required and must be 8-byte aligned
     N, R = 256, 128
     args = dict(z=4096, out=8192, packed=256 * 64, ws=256 * 128)
