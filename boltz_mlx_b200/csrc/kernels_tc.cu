@@ -860,8 +860,13 @@ cudaError_t launch_core_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
 }
 
 // =================================================================================================
-// Output projection (+ residual, optionally + the next module's LayerNorm).  CTA = 128 pairs (one
+// Output projection (+ residual, optionally + the next module's LayerNorm).  Tile = 128 pairs (one
 // query tile of one attention row): y[128 x 128] = (core o sigmoid(g))[128 x 128] * W_o^T, 256 threads.
+// The CTA loops over tiles.  Output blocks in peer GPUs' memory: a persistent grid of three CTAs per
+// SM, so the system-scope fence that publishes the remote stores runs once per CTA at the very end
+// and the stores drain while the next tiles are computed (a fence per tile held every CTA slot until
+// its 64 KB had crossed NVLink).  Local output: one tile per CTA, which the hardware's dynamic CTA
+// scheduling balances better than a static tile split.
 //   gate: warp w updates rows 16w..16w+15 of the core image; one warp instruction covers 8 rows x 4
 //     chunks of 8 channels (lane = row % 8 + 8 * (chunk % 4)): g is read in 64-byte runs of 8 rows and
 //     the image in four conflict-free 128-byte runs.
@@ -876,7 +881,7 @@ constexpr int OP_SMEM_BODY = TILE * OP_STAGE_LD * 4;  // 67584 B: covers the two
 constexpr int OP_SMEM = OP_SMEM_BODY + 64;
 static_assert(OP_SMEM_BODY >= 65536, "staging buffer overlays the operand images");
 
-template <typename T, bool LN_NEXT>
+template <typename T, bool LN_NEXT, bool PERSIST>
 __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
@@ -885,8 +890,8 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OP_SMEM_BODY);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ct = blockIdx.x, al = blockIdx.y, a = args.row_begin + al, b = blockIdx.z;
   const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT;
+  const int n_tiles = NT * R * args.B;
   int* status = args.status;
   if (tid == 0) {
     mbar_init(bars + 0, 1);
@@ -898,134 +903,151 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bars + 0, 65536);
-    bulk_g2s(sA, args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + ct) * 32768, 32768, bars + 0);
-    bulk_g2s(sW, args.packed + PackedLayout::img_o, 32768, bars + 0);
-  }
-  // ---- gate: the fp16 core image times sigmoid(g) of the same (b, row, query), rounded once to T, in
-  //      place (the MMA then reads a T image); g loads in flight before the image lands ----
-  {
-    const int r8 = lane & 7, kq = lane >> 3;
-    const unsigned char* gb = args.ws + args.wl.off_g + ((size_t)b * R + al) * N * C_IN * 2;
-    uint4 gv[8];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int r = 16 * warp + 8 * (it >> 2) + r8, k = 4 * (it & 3) + kq;
-      const int q = min(ct * TILE + r, N - 1);
-      gv[it] = __ldcs(reinterpret_cast<const uint4*>(gb + ((size_t)q * C_IN + 8 * k) * 2));
+  auto run_tile = [&](const int tile, const uint32_t par) {
+    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R), a = args.row_begin + al;
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bars + 0, 65536);
+      bulk_g2s(sA, args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + ct) * 32768, 32768, bars + 0);
+      bulk_g2s(sW, args.packed + PackedLayout::img_o, 32768, bars + 0);
     }
-    mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int r = 16 * warp + 8 * (it >> 2) + r8, k = 4 * (it & 3) + kq;
-      uint4* cp = reinterpret_cast<uint4*>(sA + img_off(r, 8 * k, HC));
-      const uint4 cv = *cp;
-      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[it].x, gv[it].y, gv[it].z, gv[it].w};
-      uint32_t ow[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 c2 = H16<__half>::unpack(cw[e]);
-        const float2 g2 = H16<T>::unpack(gw[e]);
-        ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
+    // ---- gate: the fp16 core image times sigmoid(g) of the same (b, row, query), rounded once to T, in
+    //      place (the MMA then reads a T image); g loads in flight before the image lands ----
+    {
+      const int r8 = lane & 7, kq = lane >> 3;
+      const unsigned char* gb = args.ws + args.wl.off_g + ((size_t)b * R + al) * N * C_IN * 2;
+      uint4 gv[8];
+  #pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = 16 * warp + 8 * (it >> 2) + r8, k = 4 * (it & 3) + kq;
+        const int q = min(ct * TILE + r, N - 1);
+        gv[it] = __ldcs(reinterpret_cast<const uint4*>(gb + ((size_t)q * C_IN + 8 * k) * 2));
       }
-      *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      mbar_wait(bars + 0, par, status, DEV_TIMEOUT_TMA);
+  #pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = 16 * warp + 8 * (it >> 2) + r8, k = 4 * (it & 3) + kq;
+        uint4* cp = reinterpret_cast<uint4*>(sA + img_off(r, 8 * k, HC));
+        const uint4 cv = *cp;
+        const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, gw[4] = {gv[it].x, gv[it].y, gv[it].z, gv[it].w};
+        uint32_t ow[4];
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 c2 = H16<__half>::unpack(cw[e]);
+          const float2 g2 = H16<T>::unpack(gw[e]);
+          ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
+        }
+        *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
     }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
+  #pragma unroll
+      for (int ks = 0; ks < HC / 16; ++ks) {
+        const uint64_t ad = smem_desc_noswizzle(smem_u32(sA) + ks * 256, 128, 16 * HC);
+        const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + ks * 256, 128, 16 * HC);
+        umma_ss(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(bars + 1);
+    }
+    // ---- epilogue.  Warp w streams rows 16w..16w+15 (lane: channels 4 lane..+3); the residual of its
+    //      first 8 rows is in flight during the CTA barrier that follows the staging (out may alias z:
+    //      a row's residual is always read before that row is written, and rows belong to one warp) ----
+    auto row_off = [&](const View& v, int r) -> long long {
+      return b * v.s_batch + (long long)(a - v.row0) * v.s_row + view_col(v, ct * TILE + r);
+    };
+    float4 zz[8];
+    auto load_z = [&](int h) {
+  #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = 16 * warp + 8 * h + i;
+        zz[i] = (args.add_residual && ct * TILE + r < N)
+                    ? __ldcs(reinterpret_cast<const float4*>(args.z + row_off(args.zv, r)) + lane)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    float4 lw = make_float4(0.f, 0.f, 0.f, 0.f), lb = lw;
+    if constexpr (LN_NEXT) {
+      lw = __ldg(reinterpret_cast<const float4*>(args.ln_next_w) + lane);
+      lb = __ldg(reinterpret_cast<const float4*>(args.ln_next_b) + lane);
+    }
+    mbar_wait(bars + 1, par, status, DEV_TIMEOUT_MMA);  // MMA done: the operand images are free for staging
+    __syncwarp();
     tc_fence_after();
-    constexpr uint32_t idesc = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
-#pragma unroll
-    for (int ks = 0; ks < HC / 16; ++ks) {
-      const uint64_t ad = smem_desc_noswizzle(smem_u32(sA) + ks * 256, 128, 16 * HC);
-      const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + ks * 256, 128, 16 * HC);
-      umma_ss(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
-    }
-    umma_commit(bars + 1);
-  }
-  // ---- epilogue.  Warp w streams rows 16w..16w+15 (lane: channels 4 lane..+3); the residual of its
-  //      first 8 rows is in flight during the CTA barrier that follows the staging (out may alias z:
-  //      a row's residual is always read before that row is written, and rows belong to one warp) ----
-  auto row_off = [&](const View& v, int r) -> long long {
-    return b * v.s_batch + (long long)(a - v.row0) * v.s_row + view_col(v, ct * TILE + r);
-  };
-  float4 zz[8];
-  auto load_z = [&](int h) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = 16 * warp + 8 * h + i;
-      zz[i] = (args.add_residual && ct * TILE + r < N)
-                  ? __ldcs(reinterpret_cast<const float4*>(args.z + row_off(args.zv, r)) + lane)
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  float4 lw = make_float4(0.f, 0.f, 0.f, 0.f), lb = lw;
-  if constexpr (LN_NEXT) {
-    lw = __ldg(reinterpret_cast<const float4*>(args.ln_next_w) + lane);
-    lb = __ldg(reinterpret_cast<const float4*>(args.ln_next_b) + lane);
-  }
-  mbar_wait(bars + 1, 0, status, DEV_TIMEOUT_MMA);  // MMA done: the operand images are free for staging
-  __syncwarp();
-  tc_fence_after();
-  {
-    // TMEM -> stage: warp (quad, part) holds rows 32 quad.. (its lanes), columns 64 part..
-    const int quad = warp & 3, part = warp >> 2;
-    float* srow = stage + (quad * 32 + lane) * OP_STAGE_LD + 64 * part;
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      uint32_t acc[32];
-      tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
-      tmem_ld_wait();
-      tmem_regs_ready(acc);
-#pragma unroll
-      for (int d = 0; d < 32; d += 4)
-        *reinterpret_cast<float4*>(srow + 32 * h2 + d) =
-            make_float4(__uint_as_float(acc[d]), __uint_as_float(acc[d + 1]), __uint_as_float(acc[d + 2]),
-                        __uint_as_float(acc[d + 3]));
-    }
-  }
-  load_z(0);
-  tc_fence_before();
-  __syncthreads();
-#pragma unroll 1
-  for (int h = 0; h < 2; ++h) {
-    if (h == 1) load_z(1);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = 16 * warp + 8 * h + i;
-      if (ct * TILE + r >= N) continue;  // warp-uniform
-      const float4 s = *reinterpret_cast<const float4*>(stage + r * OP_STAGE_LD + 4 * lane);
-      const float4 y = make_float4(s.x + zz[i].x, s.y + zz[i].y, s.z + zz[i].z, s.w + zz[i].w);
-      __stcs(reinterpret_cast<float4*>(args.out + row_off(args.ov, r)) + lane, y);
-      if constexpr (LN_NEXT) {
-        // the next module's LayerNorm of the new row (reference linear_addln, kernels_nax3.py:69-198):
-        // two-pass fp32 statistics, one rounding to the 16-bit type
-        const float mean = warp_sum32((y.x + y.y) + (y.z + y.w)) * (1.0f / C_IN);
-        const float d0 = y.x - mean, d1 = y.y - mean, d2 = y.z - mean, d3 = y.w - mean;
-        const float var = warp_sum32((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3)) * (1.0f / C_IN);
-        const float rstd = rsqrtf(var + LN_EPS);
-        uint2 pk;
-        pk.x = H16<T>::pack(d0 * rstd * lw.x + lb.x, d1 * rstd * lw.y + lb.y);
-        pk.y = H16<T>::pack(d2 * rstd * lw.z + lb.z, d3 * rstd * lw.w + lb.w);
-        *(reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(args.ln_out) + row_off(args.lnv, r)) + lane) = pk;
+    {
+      // TMEM -> stage: warp (quad, part) holds rows 32 quad.. (its lanes), columns 64 part..
+      const int quad = warp & 3, part = warp >> 2;
+      float* srow = stage + (quad * 32 + lane) * OP_STAGE_LD + 64 * part;
+  #pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t acc[32];
+        tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
+        tmem_ld_wait();
+        tmem_regs_ready(acc);
+  #pragma unroll
+        for (int d = 0; d < 32; d += 4)
+          *reinterpret_cast<float4*>(srow + 32 * h2 + d) =
+              make_float4(__uint_as_float(acc[d]), __uint_as_float(acc[d + 1]), __uint_as_float(acc[d + 2]),
+                          __uint_as_float(acc[d + 3]));
       }
     }
+    load_z(0);
+    tc_fence_before();
+    __syncthreads();
+  #pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1) load_z(1);
+  #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = 16 * warp + 8 * h + i;
+        if (ct * TILE + r >= N) continue;  // warp-uniform
+        const float4 s = *reinterpret_cast<const float4*>(stage + r * OP_STAGE_LD + 4 * lane);
+        const float4 y = make_float4(s.x + zz[i].x, s.y + zz[i].y, s.z + zz[i].z, s.w + zz[i].w);
+        __stcs(reinterpret_cast<float4*>(args.out + row_off(args.ov, r)) + lane, y);
+        if constexpr (LN_NEXT) {
+          // the next module's LayerNorm of the new row (reference linear_addln, kernels_nax3.py:69-198):
+          // two-pass fp32 statistics, one rounding to the 16-bit type
+          const float mean = warp_sum32((y.x + y.y) + (y.z + y.w)) * (1.0f / C_IN);
+          const float d0 = y.x - mean, d1 = y.y - mean, d2 = y.z - mean, d3 = y.w - mean;
+          const float var = warp_sum32((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3)) * (1.0f / C_IN);
+          const float rstd = rsqrtf(var + LN_EPS);
+          uint2 pk;
+          pk.x = H16<T>::pack(d0 * rstd * lw.x + lb.x, d1 * rstd * lw.y + lb.y);
+          pk.y = H16<T>::pack(d2 * rstd * lw.z + lb.z, d3 * rstd * lw.w + lb.w);
+          *(reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(args.ln_out) + row_off(args.lnv, r)) + lane) = pk;
+        }
+      }
+    }
+    // the staging rows were read through the generic proxy; the next tile's bulk copies overwrite them
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+  };
+  if constexpr (PERSIST) {
+#pragma unroll 1
+    for (int tile = blockIdx.x, iter = 0; tile < n_tiles; tile += gridDim.x, ++iter) run_tile(tile, iter & 1);
+  } else {
+    run_tile(blockIdx.x, 0);
   }
   // peer stores (output blocks in other GPUs' memory): performed system-wide before the kernel ends,
   // ahead of the cross-GPU barrier that publishes them
   if (args.ov.tab || args.lnv.tab) __threadfence_system();
-  __syncthreads();
   if (warp == 0) tmem_dealloc(tbase, 128);
 }
 
 template <typename T, bool LN_NEXT>
 static cudaError_t out_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
-  cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
-  const int R = a.row_end - a.row_begin;
-  dim3 grid(a.wl.NT, R, a.B);
-  out_proj_tc_kernel<T, LN_NEXT><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
+  const int n_tiles = a.wl.NT * (a.row_end - a.row_begin) * a.B;
+  if (a.ov.tab || a.lnv.tab) {  // output blocks on peer GPUs: persistent, three resident CTAs per SM
+    cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
+    const int grid = n_tiles < 3 * a.num_sms ? n_tiles : 3 * a.num_sms;
+    out_proj_tc_kernel<T, LN_NEXT, true><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
+  } else {
+    cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
+    out_proj_tc_kernel<T, LN_NEXT, false><<<n_tiles, OP_THREADS, OP_SMEM, st>>>(a);
+  }
   return cudaGetLastError();
 }
 
