@@ -23,7 +23,7 @@ EXPORTED = [
     "triattn_ln_proj", "triattn_core", "triattn_out_proj", "triattn_mask_prep_v", "triattn_ln_proj_v",
     "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb", "triattn_forward_fused",
     "triattn_out_proj_vt", "triattn_peer_alloc", "triattn_peer_free", "triattn_ipc_handle", "triattn_ipc_open",
-    "triattn_ipc_close", "triattn_peer_barrier", "triattn_peer_broadcast",
+    "triattn_ipc_close", "triattn_peer_barrier", "triattn_peer_broadcast", "triattn_forward_chunked",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -65,6 +65,7 @@ def lib() -> ctypes.CDLL:
         L.triattn_workspace_bytes.restype = _sz
         L.triattn_workspace_bytes.argtypes = [_i, _i, _i, _i]
         L.triattn_forward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _vp, _sz, _vp]
+        L.triattn_forward_chunked.argtypes = [_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _i, _vp, _sz, _vp]
         L.triattn_forward_fused.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _i, _vp, _vp, _vp, _i,
                                             _vp, _sz, _vp]
         L.triattn_mask_prep.argtypes = [_vp, _i, _i, _i, _f, _i, _i, _i, _vp, _sz, _vp]

@@ -470,4 +470,52 @@ int triattn_forward(const float* z, const float* mask, const void* packed, int B
   return TRIATTN_OK;
 }
 
+int triattn_forward_chunked(const float* z, const float* mask, const void* packed, int B, int N, int starting,
+                            float inf, int dtype, int add_residual, float* out, int chunk_rows, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if (!z || !aligned(z, 16)) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
+  if (!out || !aligned(out, 16)) return fail(TRIATTN_EINVAL, "out must be a 16-byte aligned device pointer");
+  if (int r = check_packed(packed, dtype)) return r;
+  if (chunk_rows < 1) return fail(TRIATTN_EINVAL, "chunk_rows=%d must be >= 1", chunk_rows);
+  const int C = chunk_rows < N ? chunk_rows : N;
+  if (dtype != DT_F32 && C < N && C % TILE)
+    return fail(TRIATTN_EINVAL, "16-bit chunks hold whole 128-row tri-bias blocks: chunk_rows=%d", chunk_rows);
+  if (int r = check_ws(workspace, workspace_bytes, Workspace::make(B, N, C, dtype))) return r;
+  int* status = device_status_ptr();
+  if (!status) return fail(TRIATTN_ECUDA, "device status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nch = (N + C - 1) / C;
+  auto args_of = [&](int k) {
+    const int r0 = k * C, r1 = r0 + C < N ? r0 + C : N;
+    return make_args(B, N, starting, r0, r1, inf, z, mask, out, add_residual, packed, workspace, dtype);
+  };
+  auto ln_proj = [&](const LayerArgs& a) {
+    return dtype == DT_F32 ? launch_ln_proj_f32(a, st) : launch_ln_proj_tc(a, dtype, st);
+  };
+  // pass 1: the tri-bias rows of every chunk (the bias region is shared by all row counts); each
+  // chunk's q|k|v|g rows land in the per-row regions and are overwritten by the next chunk
+  for (int k = 0; k < nch; ++k) {
+    cudaError_t e = ln_proj(args_of(k));
+    if (e != cudaSuccess) return cuda_fail(e, "ln_proj (tri-bias pass)");
+  }
+  // pass 2, last chunk first: its projections from pass 1 are still in the workspace.  With out == z
+  // (in place) a chunk writes only its own attention rows (ending node: its columns of z), which no
+  // later chunk reads.
+  for (int k = nch - 1; k >= 0; --k) {
+    const LayerArgs a = args_of(k);
+    cudaError_t e = launch_mask_prep(a, dtype, st);
+    if (e != cudaSuccess) return cuda_fail(e, "mask_prep");
+    if (k != nch - 1) {
+      e = ln_proj(a);
+      if (e != cudaSuccess) return cuda_fail(e, "ln_proj");
+    }
+    e = dtype == DT_F32 ? launch_core_f32(a, st) : launch_core_tc(a, dtype, st);
+    if (e != cudaSuccess) return cuda_fail(e, "core");
+    e = dtype == DT_F32 ? launch_out_proj_f32(a, st) : launch_out_proj_tc(a, dtype, st);
+    if (e != cudaSuccess) return cuda_fail(e, "out_proj");
+  }
+  return TRIATTN_OK;
+}
+
 }  // extern "C"

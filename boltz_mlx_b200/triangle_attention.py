@@ -25,6 +25,7 @@ import torch
 from torch import nn
 
 from . import _lib
+from .layout import workspace_bytes
 
 
 class Attention(nn.Module):
@@ -105,9 +106,30 @@ class TriangleAttention(nn.Module):
                 _lib.EUNSUPPORTED,
                 f"the sm_100a kernels implement c_in=128, 4 heads x 32 (got {self.c_in}, {self.no_heads}x{self.c_hidden})")
 
+    # Workspace budget of one call: a layer whose full workspace is larger runs row-chunked (the tri
+    # bias of all rows, then chunks of rows; attention.py:55-68).  At B = 1, 16-bit: N = 2048 needs
+    # 5.4 GB and runs whole; N = 4096 needs 21 GB and runs in chunks.
+    max_workspace_bytes: int = 8 << 30
+
+    def chunk_rows(self, B: int, N: int, dtype: int, chunk_size: Optional[int] = None) -> int:
+        """Rows per chunk for a B x N layer: `chunk_size` rounded up to a whole 128-row tile on the
+        16-bit path, or (None) all N rows when the workspace fits max_workspace_bytes, else the
+        largest multiple of 128 rows that fits (at least 128)."""
+        if chunk_size is not None:
+            if chunk_size < 1:
+                raise ValueError(f"chunk_size must be >= 1, got {chunk_size}")
+            c = chunk_size if dtype == _lib.F32 else -(-chunk_size // 128) * 128
+            return min(c, N)
+        if workspace_bytes(B, N, N, dtype) <= self.max_workspace_bytes:
+            return N
+        c = 128
+        while c + 128 < N and workspace_bytes(B, N, c + 128, dtype) <= self.max_workspace_bytes:
+            c += 128
+        return min(c, N)
+
     # ---- calls ------------------------------------------------------------------------------
     def _run(self, x: torch.Tensor, mask: Optional[torch.Tensor], add_residual: bool,
-             out: Optional[torch.Tensor]) -> torch.Tensor:
+             out: Optional[torch.Tensor], chunk_size: Optional[int] = None) -> torch.Tensor:
         self._check_geometry()
         if not x.is_cuda:
             raise RuntimeError("TriangleAttention (B200) needs CUDA tensors; there is no CPU path")
@@ -124,23 +146,33 @@ class TriangleAttention(nn.Module):
         if out is None:
             out = torch.empty_like(z)
         packed = self.packed_weights(dtype)
-        nbytes = _lib.workspace_bytes(B, N, N, dtype)
+        rows = self.chunk_rows(B, N, dtype, chunk_size)
+        nbytes = _lib.workspace_bytes(B, N, rows, dtype)
         ws = self._ws.get(nbytes, z.device)
-        _lib.check(_lib.lib().triattn_forward(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N, int(self.starting),
-                                              float(self.inf), dtype, int(add_residual), out.data_ptr(),
-                                              ws.data_ptr(), ws.numel(), _lib.stream_handle(z.device)))
+        if rows == N:
+            _lib.check(_lib.lib().triattn_forward(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N,
+                                                  int(self.starting), float(self.inf), dtype, int(add_residual),
+                                                  out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                  _lib.stream_handle(z.device)))
+        else:
+            _lib.check(_lib.lib().triattn_forward_chunked(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N,
+                                                          int(self.starting), float(self.inf), dtype,
+                                                          int(add_residual), out.data_ptr(), rows, ws.data_ptr(),
+                                                          ws.numel(), _lib.stream_handle(z.device)))
         return out
 
     def forward(self, x: torch.Tensor, mask: Optional[torch.Tensor] = None, chunk_size: Optional[int] = None,
                 use_kernels: bool = False, xn: Optional[torch.Tensor] = None, keep_t: bool = False) -> torch.Tensor:
         """x [B, I, J, c_in] -> update y [B, I, J, c_in] (same orientation as x).
 
-        `chunk_size` / `use_kernels` are accepted and ignored, as in the reference.  As in the reference's
+        `chunk_size`: rows per chunk of the row-chunked layer (None: automatic, whole layer unless its
+        workspace exceeds max_workspace_bytes); the result is the same bit for bit either way.
+        `use_kernels` is accepted and ignored, as in the reference.  As in the reference's
         f16 path (attention.py:95-103): `xn` = this module's LayerNorm output already computed (16-bit, the
         module's type; for the ending node already transposed), so the LayerNorm is skipped; `keep_t` =
         return the ending node's update in the transposed layout."""
         if xn is None and not keep_t:
-            return self._run(x, mask, False, None)
+            return self._run(x, mask, False, None, chunk_size)
         return self._run_fused(x, mask, xn, add_residual=False, keep_t=keep_t)[0]
 
     def f16_addln(self, z: torch.Tensor, mask: Optional[torch.Tensor], xn: Optional[torch.Tensor], ln_next,
@@ -203,11 +235,11 @@ class TriangleAttention(nn.Module):
         return out, ln_out
 
     def forward_residual(self, z: torch.Tensor, mask: Optional[torch.Tensor] = None, *,
-                         inplace: bool = False) -> torch.Tensor:
+                         inplace: bool = False, chunk_size: Optional[int] = None) -> torch.Tensor:
         """z + self(z) in one pass (the pairformer's residual update, pairformer.py:86-87)."""
         zc = z.contiguous()
         out = zc if (inplace and zc is z and z.dtype == torch.float32) else None
-        return self._run(zc, mask, True, out)
+        return self._run(zc, mask, True, out, chunk_size)
 
 
 TriangleAttentionStartingNode = TriangleAttention

@@ -104,6 +104,19 @@ TRIATTN_API int triattn_forward(const float* z, const float* mask, const void* p
                     float inf, int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* Row-chunked form of triattn_forward for large N (bounded memory) <- the reference's chunked layer
+ * (attention.py:55-68: the tri bias from ALL rows, then the attention core over row chunks): pass 1
+ * runs the LayerNorm + projection of every chunk for its tri-bias rows, pass 2 runs mask bias,
+ * LayerNorm + projection, core and output projection chunk by chunk.  The workspace covers
+ * chunk_rows rows only: triattn_workspace_bytes(B, N, chunk_rows, dtype) (the tri-bias region, which
+ * always spans all N rows, plus chunk_rows rows of per-row regions).  chunk_rows >= N is one chunk;
+ * on the 16-bit path a smaller chunk_rows must be a multiple of 128.  Results equal
+ * triattn_forward's bit for bit (identical per-row arithmetic); out may alias z (add_residual = 1).
+ * All offsets are 64-bit: N up to 16384 (z alone is 137 GB there). */
+TRIATTN_API int triattn_forward_chunked(const float* z, const float* mask, const void* packed, int B, int N,
+                                        int starting, float inf, int dtype, int add_residual, float* out,
+                                        int chunk_rows, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- stages (row-range granularity: the reference's row chunking, attention.py:55-68) ------
  * All stages address attention rows a in [row_begin, row_end) of the full-size z / mask / out. */
 
