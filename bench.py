@@ -493,6 +493,78 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+def trimul_flops(N: int, B: int = 1) -> dict:
+    """Triangle multiplication per layer: the per-channel contraction 2 N^3 D, the projections
+    2 N^2 D (4D + D) (p_in | g_in | g_out) and 2 N^2 D D (p_out)."""
+    contraction = 2 * B * N ** 3 * CZ
+    proj = 2 * B * N * N * CZ * (5 * CZ) + 2 * B * N * N * CZ * CZ
+    return {"contraction": contraction, "proj": proj, "total": contraction + proj}
+
+
+def run_trimul(args):
+    """--layer trimul: one step = TriangleMultiplicationOutgoing then Incoming, each with its residual
+    (the pairformer block's order), on the config's synthetic pair tensor and mask."""
+    from boltz_mlx_b200 import TriangleMultiplicationIncoming, TriangleMultiplicationOutgoing, _lib, load_trimul_params
+
+    def tm_params(seed):  # linears ~ N(0, 1/128), LayerNorm affine near identity
+        g = torch.Generator().manual_seed(seed)
+        p = {k: torch.randn(2 * CZ, CZ, generator=g) / CZ ** 0.5 for k in ("p_in", "g_in")}
+        p.update({k: torch.randn(CZ, CZ, generator=g) / CZ ** 0.5 for k in ("p_out", "g_out")})
+        for k in ("in", "out"):
+            p[f"{k}_w"] = 1.0 + 0.1 * torch.randn(CZ, generator=g)
+            p[f"{k}_b"] = 0.1 * torch.randn(CZ, generator=g)
+        return p
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    N = cfg["N"]
+    prec = args.precision or cfg["dtype"]
+    z_h, pm_h, _, _ = make_config_inputs(args.config)
+    mods = [load_trimul_params(cls(128, precision=prec).to(dev), tm_params(cfg["seed_w"] + 50 + i))
+            for i, cls in enumerate((TriangleMultiplicationOutgoing, TriangleMultiplicationIncoming))]
+    z, mask = z_h.to(dev), pm_h.to(dev)
+    t1, t2 = torch.empty_like(z), torch.empty_like(z)
+
+    def step():
+        torch.add(z, 0, out=t1)  # every step starts from the same input (the layers update in place)
+        mods[0].forward_residual(t1, mask, inplace=True)
+        mods[1].forward_residual(t1, mask, inplace=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu_index(0)) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    # the input copy (one N^2 x 512 B device copy per step) timed alone and taken out
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for _ in range(args.steps):
+        torch.add(z, 0, out=t2)
+    c1.record(stream)
+    torch.cuda.synchronize()
+    step_ms = (ev0.elapsed_time(ev1) - c0.elapsed_time(c1)) / args.steps
+    fl = trimul_flops(N)
+    line = {
+        "metric": f"tri-mult TFLOP/s, outgoing+incoming pair, N={N}, B=1", "layer": "trimul",
+        "value": 2 * fl["total"] / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "ms_per_layer": step_ms / 2, "higher_is_better": True,
+        "dtype": prec, "data": "synthetic: the config's pair tensor and mask, seeded N(0,1/128) weights",
+        "config": {"workload": f"config{args.config}: tri-mult outgoing + incoming, N={N}, c_z=128, {prec}",
+                   "N": N, "flops_per_layer": fl, "note": "input copy per step timed separately and subtracted"},
+        "device_status": _lib.device_status(), "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_stack(args):
     """Config 3 line: sustained ms per layer of the 128-layer 16-bit stack and its drift against the
     same stack through the fp32 path."""
@@ -543,6 +615,9 @@ def main():
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU block exchange: peer stores from the output projection + cross-GPU barrier "
                          "(default), or NCCL all-to-alls")
+    ap.add_argument("--layer", default="triattn", choices=["triattn", "trimul"],
+                    help="triattn: the north-star start+end pair (default); trimul: triangle multiplication "
+                         "outgoing + incoming on the same config (single GPU)")
     ap.add_argument("--case", type=int, default=None,
                     help="profiling case: run one start+end pair at this N once (after one warm-up pair), "
                          "check the device status and exit; nothing is timed")
@@ -552,7 +627,9 @@ def main():
         return
     if args.config is None:
         args.config = 2  # one workload for every GPU count, so the driver's scaling ratios compare like with like
-    if args.impl == "b200" and "blocks" in CONFIGS[args.config]:
+    if args.layer == "trimul":
+        run_trimul(args)
+    elif args.impl == "b200" and "blocks" in CONFIGS[args.config]:
         run_stack(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -13,9 +13,15 @@ from .triangle_attention import (  # noqa: F401
     load_params,
     pack_weights,
 )
+from .triangle_mult import (  # noqa: F401
+    TriangleMultiplicationIncoming,
+    TriangleMultiplicationOutgoing,
+    load_trimul_params,
+)
 from . import _lib  # noqa: F401
 from .weights import load_module, load_pairformer_triatt, read_safetensors, write_safetensors  # noqa: F401
 
 __all__ = ["Attention", "TriangleAttention", "TriangleAttentionStartingNode", "TriangleAttentionEndingNode",
            "load_params", "pack_weights", "read_safetensors", "write_safetensors", "load_module",
-           "load_pairformer_triatt"]
+           "load_pairformer_triatt", "TriangleMultiplicationOutgoing", "TriangleMultiplicationIncoming",
+           "load_trimul_params"]

@@ -24,6 +24,8 @@ EXPORTED = [
     "triattn_out_proj_v", "triattn_ln_proj_vb", "triattn_out_proj_vb", "triattn_forward_fused",
     "triattn_out_proj_vt", "triattn_peer_alloc", "triattn_peer_free", "triattn_ipc_handle", "triattn_ipc_open",
     "triattn_ipc_close", "triattn_peer_barrier", "triattn_peer_broadcast", "triattn_forward_chunked",
+    "triattn_trimul_packed_bytes", "triattn_trimul_pack_weights", "triattn_trimul_workspace_bytes",
+    "triattn_trimul_forward",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -89,9 +91,16 @@ def lib() -> ctypes.CDLL:
         L.triattn_ipc_close.argtypes = [_vp]
         L.triattn_peer_barrier.argtypes = [_vp, _i, _i, ctypes.c_uint32, _vp]
         L.triattn_peer_broadcast.argtypes = [_vp, _i, _i, _sz, _sz, _vp]
+        L.triattn_trimul_packed_bytes.restype = _sz
+        L.triattn_trimul_packed_bytes.argtypes = [_i]
+        L.triattn_trimul_workspace_bytes.restype = _sz
+        L.triattn_trimul_workspace_bytes.argtypes = [_i, _i, _i]
+        L.triattn_trimul_pack_weights.argtypes = [_vp] * 8 + [_i, _vp, _sz, _vp]
+        L.triattn_trimul_forward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]
         for name in EXPORTED:
             if name not in ("triattn_version", "triattn_last_error_string", "triattn_packed_weights_bytes",
-                            "triattn_workspace_bytes"):
+                            "triattn_workspace_bytes", "triattn_trimul_packed_bytes",
+                            "triattn_trimul_workspace_bytes"):
                 getattr(L, name).restype = ctypes.c_int
         _L = L
     return _L

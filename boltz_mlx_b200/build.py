@@ -14,7 +14,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libtriattn.so"
-SOURCES = ["capi.cu", "kernels_f32.cu", "kernels_tc.cu", "noalloc.cu", "peer.cu"]
+SOURCES = ["capi.cu", "kernels_f32.cu", "kernels_tc.cu", "noalloc.cu", "peer.cu", "trimul.cu"]
 HEADERS = ["sm100.cuh", "triattn_internal.cuh"]
 
 NVCC_FLAGS = [
@@ -24,6 +24,7 @@ NVCC_FLAGS = [
     "-shared", "-cudart", "shared",
     "-Xlinker", "-rpath,/usr/local/cuda/lib64",
     "--expt-relaxed-constexpr",
+    "-lcublas",
 ]
 
 

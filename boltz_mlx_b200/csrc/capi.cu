@@ -470,6 +470,54 @@ int triattn_forward(const float* z, const float* mask, const void* packed, int B
   return TRIATTN_OK;
 }
 
+// ---- triangle multiplication ---------------------------------------------------------------------
+size_t triattn_trimul_packed_bytes(int dtype) { return TrimulPacked::bytes(dtype); }
+
+size_t triattn_trimul_workspace_bytes(int B, int N, int dtype) {
+  if (B < 1 || N < 1) return 0;
+  return TrimulWorkspace::make(B, N, dtype).total;
+}
+
+int triattn_trimul_pack_weights(const float* in_w, const float* in_b, const float* p_in, const float* g_in,
+                                const float* out_w, const float* out_b, const float* p_out, const float* g_out,
+                                int dtype, void* packed, size_t packed_bytes, void* stream) {
+  if (!in_w || !in_b || !p_in || !g_in || !out_w || !out_b || !p_out || !g_out)
+    return fail(TRIATTN_EINVAL, "trimul_pack_weights: a parameter pointer is NULL");
+  if (dtype != DT_F32 && dtype != DT_F16 && dtype != DT_BF16) return fail(TRIATTN_EUNSUPPORTED, "dtype %d", dtype);
+  if (!packed || !aligned(packed, 256)) return fail(TRIATTN_EINVAL, "packed must be a 256-byte aligned device pointer");
+  if (packed_bytes < TrimulPacked::bytes(dtype))
+    return fail(TRIATTN_ENOSPACE, "packed %zu bytes < %zu needed", packed_bytes, TrimulPacked::bytes(dtype));
+  if (!aligned(in_w, 16) || !aligned(in_b, 16) || !aligned(out_w, 16) || !aligned(out_b, 16))
+    return fail(TRIATTN_EINVAL, "LayerNorm parameters must be 16-byte aligned");
+  return finish(launch_trimul_pack(in_w, in_b, p_in, g_in, out_w, out_b, p_out, g_out, dtype,
+                                   static_cast<unsigned char*>(packed), static_cast<cudaStream_t>(stream)),
+                "trimul_pack_weights");
+}
+
+int triattn_trimul_forward(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
+                           int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (int r = check_dims(B, N, dtype)) return r;
+  if ((long long)B * N * N > 2147483647LL) return fail(TRIATTN_EUNSUPPORTED, "B*N*N above 2^31 pairs");
+  if (!z || !aligned(z, 16)) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
+  if (!out || !aligned(out, 16)) return fail(TRIATTN_EINVAL, "out must be a 16-byte aligned device pointer");
+  if (int r = check_packed(packed, dtype)) return r;
+  const TrimulWorkspace wl = TrimulWorkspace::make(B, N, dtype);
+  if (!workspace || !aligned(workspace, 256)) return fail(TRIATTN_EINVAL, "workspace must be 256-byte aligned");
+  if (workspace_bytes < wl.total)
+    return fail(TRIATTN_ENOSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, wl.total);
+  TrimulArgs a{};
+  a.z = z; a.mask = mask; a.packed = static_cast<const unsigned char*>(packed);
+  a.B = B; a.N = N; a.outgoing = outgoing ? 1 : 0; a.dtype = dtype; a.add_residual = add_residual ? 1 : 0;
+  a.out = out; a.ws = static_cast<unsigned char*>(workspace);
+  int blas = 0;
+  const char* stage = "";
+  const cudaError_t e = launch_trimul(a, static_cast<cudaStream_t>(stream), &blas, &stage);
+  if (blas) return fail(TRIATTN_ECUDA, "trimul %s: cuBLAS status %d", stage, blas);
+  if (e != cudaSuccess) return fail(TRIATTN_ECUDA, "trimul %s: %s", stage, cudaGetErrorString(e));
+  return TRIATTN_OK;
+}
+
 int triattn_forward_chunked(const float* z, const float* mask, const void* packed, int B, int N, int starting,
                             float inf, int dtype, int add_residual, float* out, int chunk_rows, void* workspace,
                             size_t workspace_bytes, void* stream) {

@@ -94,6 +94,50 @@ struct Workspace {
   }
 };
 
+// ---- triangle multiplication (outgoing / incoming edges) -----------------------------------------
+// packed weights: fp32 section: in_w, in_b, out_w, out_b [128 each]; W1 = p_in | g_in | g_out
+// [640][128]; p_out [128][128].  16-bit section (16-bit modes): W1 and p_out in the layer's type.
+constexpr int TM_D = 128;
+constexpr int TM_W1 = 5 * TM_D;  // 640 = p_in (256) | g_in (256) | g_out (128)
+struct TrimulPacked {
+  static constexpr size_t in_w = 0, in_b = 512, out_w = 1024, out_b = 1536;
+  static constexpr size_t w1 = 2048;
+  static constexpr size_t p_out = w1 + (size_t)TM_W1 * TM_D * 4;
+  static constexpr size_t f32_end = p_out + (size_t)TM_D * TM_D * 4;
+  static constexpr size_t w1_16 = align_up(f32_end, 256);
+  static constexpr size_t p_out_16 = w1_16 + (size_t)TM_W1 * TM_D * 2;
+  static constexpr size_t end16 = p_out_16 + (size_t)TM_D * TM_D * 2;
+  static constexpr size_t bytes(int dtype) { return dtype == DT_F32 ? align_up(f32_end, 256) : align_up(end16, 256); }
+};
+// workspace of one call over P = B*N*N pairs (es = element size of the layer's type):
+//   xn  [P][128]      LayerNorm-in output (es); later norm_out's output (same place)
+//   h   [P][640]      projection p | g | g_out (es)
+//   ab  [2][B][128][N][N]  gated + masked a, b, channel-major (es); later p_out's output [P][128] fp32
+//   o   [B][128][N][N]     contraction output, fp32, channel-major
+//   blas                   32 MiB scratch handed to cuBLAS
+struct TrimulWorkspace {
+  size_t off_xn, off_h, off_ab, off_o, off_blas, total;
+  static constexpr size_t BLAS_BYTES = 32ull << 20;
+  __host__ __device__ static TrimulWorkspace make(int B, int N, int dtype) {
+    TrimulWorkspace w{};
+    const size_t P = (size_t)B * N * N, es = dtype == DT_F32 ? 4 : 2, A = 256;
+    size_t o = 0;
+    w.off_xn = o; o = align_up(o + P * TM_D * es, A);
+    w.off_h = o; o = align_up(o + P * TM_W1 * es, A);
+    const size_t ab = 2 * P * TM_D * es, po = P * TM_D * 4;
+    w.off_ab = o; o = align_up(o + (ab > po ? ab : po), A);
+    w.off_o = o; o = align_up(o + P * TM_D * 4, A);
+    w.off_blas = o; o = align_up(o + BLAS_BYTES, A);
+    w.total = o;
+    return w;
+  }
+};
+struct TrimulArgs {
+  const float* z; const float* mask; const unsigned char* packed;
+  int B, N, outgoing, dtype, add_residual;
+  float* out; unsigned char* ws;
+};
+
 // Byte offset of tri-bias element (q, k) of head h, batch b on the 16-bit path.
 __host__ __device__ __forceinline__ size_t bias16_off(int q, int k, int b, int h, int B, int NT) {
   const size_t blk = (((size_t)(q >> 7) * B + b) * HEADS + h) * NT + (k >> 7);
@@ -163,6 +207,11 @@ cudaError_t launch_peer_barrier(const unsigned long long* flag_ptrs, int rank, i
                                 int* status, cudaStream_t st);
 cudaError_t launch_peer_broadcast(const unsigned long long* dst_ptrs, int rank, int world, size_t offset, size_t bytes,
                                   int num_sms, cudaStream_t st);
+cudaError_t launch_trimul_pack(const float* in_w, const float* in_b, const float* p_in, const float* g_in,
+                               const float* out_w, const float* out_b, const float* p_out, const float* g_out,
+                               int dtype, unsigned char* packed, cudaStream_t st);
+// the layer: 4 kernels + 3 cuBLAS GEMMs; a cuBLAS failure returns cudaErrorUnknown with *blas_status set
+cudaError_t launch_trimul(const TrimulArgs& a, cudaStream_t st, int* blas_status, const char** stage);
 int* device_status_ptr();
 int record_error(int code, const char* what, const char* detail);
 

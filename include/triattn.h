@@ -231,6 +231,27 @@ TRIATTN_API int triattn_out_proj(const float* z, const void* packed, int B, int 
                      int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* ---- triangle multiplication (the pairformer's other O(N^3) pair op) -----------------------
+ * TriangleMultiplicationOutgoing / Incoming <- boltz_mlx/layers/triangular_mult.py:10-178 (fp32 ops
+ * path :23-49; parameters norm_in.{weight,bias}, p_in.weight [256,128], g_in.weight [256,128],
+ * norm_out.{weight,bias}, p_out.weight [128,128], g_out.weight [128,128], no biases):
+ *   xn = norm_in(z); a|b = p_in(xn) * sigmoid(g_in(xn)) * mask
+ *   outgoing o[i,j,d] = sum_k a[i,k,d] b[j,k,d];  incoming o[i,j,d] = sum_k a[k,i,d] b[k,j,d]
+ *   out = (z +) p_out(norm_out(o)) * sigmoid(g_out(xn))
+ * dtype: TRIATTN_F32 (every step fp32) or a 16-bit type (operands 16-bit, fp32 accumulation, fp32 o).
+ * mask may be NULL (ones); out may alias z with add_residual = 1.  B*N*N must stay below 2^31.
+ * The contraction and the projections run as cuBLAS GEMMs on `stream`, with the workspace's last 32
+ * MiB as cuBLAS scratch (the first call on a device creates its cuBLAS handle). */
+TRIATTN_API size_t triattn_trimul_packed_bytes(int dtype);
+TRIATTN_API int triattn_trimul_pack_weights(const float* in_w, const float* in_b, const float* p_in,
+                                            const float* g_in, const float* out_w, const float* out_b,
+                                            const float* p_out, const float* g_out, int dtype, void* packed,
+                                            size_t packed_bytes, void* stream);
+TRIATTN_API size_t triattn_trimul_workspace_bytes(int B, int N, int dtype);
+TRIATTN_API int triattn_trimul_forward(const float* z, const float* mask, const void* packed, int B, int N,
+                                       int outgoing, int dtype, int add_residual, float* out, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /* ---- allocation-free layer ----------------------------------------------------------------
  * No counterpart in the reference.  triattn_forward without a workspace argument, for callers that
  * cannot allocate device memory at run time (a plugin host that forbids cudaMalloc after start-up,
