@@ -96,7 +96,9 @@ struct Workspace {
 
 // ---- triangle multiplication (outgoing / incoming edges) -----------------------------------------
 // packed weights: fp32 section: in_w, in_b, out_w, out_b [128 each]; W1 = p_in | g_in | g_out
-// [640][128]; p_out [128][128].  16-bit section (16-bit modes): W1 and p_out in the layer's type.
+// [640][128]; p_out [128][128].  16-bit section (16-bit modes): W1 and p_out in the layer's type,
+// row-major (cuBLAS operands), and the p_in | g_in rows (512 x 128) once more as a K-major no-swizzle
+// UMMA operand image (img_off) for the fused projection kernel.
 constexpr int TM_D = 128;
 constexpr int TM_W1 = 5 * TM_D;  // 640 = p_in (256) | g_in (256) | g_out (128)
 struct TrimulPacked {
@@ -106,12 +108,14 @@ struct TrimulPacked {
   static constexpr size_t f32_end = p_out + (size_t)TM_D * TM_D * 4;
   static constexpr size_t w1_16 = align_up(f32_end, 256);
   static constexpr size_t p_out_16 = w1_16 + (size_t)TM_W1 * TM_D * 2;
-  static constexpr size_t end16 = p_out_16 + (size_t)TM_D * TM_D * 2;
+  static constexpr size_t img_pg = align_up(p_out_16 + (size_t)TM_D * TM_D * 2, 1024);
+  static constexpr size_t end16 = img_pg + (size_t)4 * TM_D * TM_D * 2;
   static constexpr size_t bytes(int dtype) { return dtype == DT_F32 ? align_up(f32_end, 256) : align_up(end16, 256); }
 };
 // workspace of one call over P = B*N*N pairs (es = element size of the layer's type):
 //   xn  [P][128]      LayerNorm-in output (es); later norm_out's output (same place)
-//   h   [P][640]      projection p | g | g_out (es)
+//   h   fp32 mode: [P][640] projection p | g | g_out; 16-bit modes: [P][128] g_out only (the fused
+//       projection kernel gates a and b in its epilogue and never writes p, g)
 //   ab  [2][B][128][N][N]  gated + masked a, b, channel-major (es); later p_out's output [P][128] fp32
 //   o   [B][128][N][N]     contraction output, fp32, channel-major
 //   blas                   32 MiB scratch handed to cuBLAS
@@ -123,7 +127,7 @@ struct TrimulWorkspace {
     const size_t P = (size_t)B * N * N, es = dtype == DT_F32 ? 4 : 2, A = 256;
     size_t o = 0;
     w.off_xn = o; o = align_up(o + P * TM_D * es, A);
-    w.off_h = o; o = align_up(o + P * TM_W1 * es, A);
+    w.off_h = o; o = align_up(o + P * (dtype == DT_F32 ? TM_W1 : TM_D) * es, A);
     const size_t ab = 2 * P * TM_D * es, po = P * TM_D * 4;
     w.off_ab = o; o = align_up(o + (ab > po ? ab : po), A);
     w.off_o = o; o = align_up(o + P * TM_D * 4, A);

@@ -1,9 +1,15 @@
 // Triangle multiplication, outgoing and incoming edges (boltz_mlx/layers/triangular_mult.py:10-178),
 // forward only, on a B200:
 //
+//   16-bit modes:
+//   F1  tm_proj_tc (tcgen05): LayerNorm-in -> UMMA with [p_in | g_in] (512 x 128) -> a = p sigmoid(g) m,
+//       b likewise, stored channel-major [B][128][N][N] from the epilogue; xn [P][128] as a by-product
+//   G1  cuBLAS GEMM   g_out = xn . g_out_w^T                              -> [P][128]
+//   fp32 mode:
 //   K1  LayerNorm-in, one warp per pair (two-pass fp32 statistics)      z fp32 -> xn [P][128]
 //   G1  cuBLAS GEMM   h = xn . [p_in | g_in | g_out]^T                  -> h [P][640]
 //   K2  gate + mask, transposed through shared memory to channel-major  -> a, b [B][128][N][N]
+//   both:
 //   G2  cuBLAS strided-batched GEMM, one N x N x N product per (batch, channel):
 //         outgoing  o = a . b^T  (o[i,j] = sum_k a[i,k] b[j,k])
 //         incoming  o = a^T . b  (o[i,j] = sum_k a[k,i] b[k,j])                -> o fp32 [B][128][N][N]
@@ -161,13 +167,13 @@ __global__ void __launch_bounds__(256) tm_ln_out_kernel(const float* __restrict_
 // ---- K4: out = (z) + y * sigmoid(g_out) (triangular_mult.py:49 and the pairformer's residual) ----
 template <typename T>
 __global__ void __launch_bounds__(256) tm_out_kernel(const float* z, const float* __restrict__ y,
-                                                     const T* __restrict__ h, float* out, long long n4,
-                                                     int add_residual) {
+                                                     const T* __restrict__ gout, int g_stride, float* out,
+                                                     long long n4, int add_residual) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
     const long long p = i >> 5, c = (i & 31) * 4;  // 32 float4 per pair
     const float4 yv = __ldcs(reinterpret_cast<const float4*>(y) + i);
-    const float4 g = Ew<T>::ld4(h + p * TM_W1 + 4 * TM_D + c);
+    const float4 g = Ew<T>::ld4(gout + p * g_stride + c);
     float4 r = make_float4(yv.x * tm_sigmoid(g.x), yv.y * tm_sigmoid(g.y), yv.z * tm_sigmoid(g.z),
                            yv.w * tm_sigmoid(g.w));
     if (add_residual) {
@@ -176,6 +182,150 @@ __global__ void __launch_bounds__(256) tm_out_kernel(const float* z, const float
     }
     reinterpret_cast<float4*>(out)[i] = r;
   }
+}
+
+// ---- F1 (16-bit modes): fused LayerNorm-in + [p_in | g_in] projection + gate/mask epilogue --------
+// Persistent, one CTA per SM (512 threads), the 128 KB operand image of [p_in | g_in] loaded once.
+// Tile = 128 consecutive pairs.  Per tile: LayerNorm (warp w: pairs 8w..8w+7, lane: channels
+// 4 lane..+3) into a 128-byte-swizzled operand image and, as a by-product, xn to global memory (the
+// g_out GEMM's operand); UMMA D[128 x 512] = xn [p_in | g_in]^T in two N = 256 halves (p | g, TMEM
+// columns 0..255 | 256..511); epilogue: warp (quad, tt) takes TMEM lanes 32 quad.. and channels
+// 64 tt.. of a|b, a = p sigmoid(g) m, written channel-major (a warp's 32 lanes are 32 consecutive
+// pairs of one channel row: 64-byte runs).  The LayerNorm of tile it + 1 runs while the MMA of tile it
+// executes (two operand images), as in the attention projection kernel.
+constexpr int TP_THREADS = 512;
+constexpr int TP_W_BYTES = 4 * TM_D * TM_D * 2;  // 512 x 128 16-bit image
+constexpr int TP_A_BYTES = TILE * TM_D * 2;      // one 128-pair LayerNorm image
+constexpr int TP_SMEM = TP_W_BYTES + 2 * TP_A_BYTES + 64;
+
+template <typename T>
+__global__ void __launch_bounds__(TP_THREADS, 1)
+    tm_proj_tc_kernel(const float* __restrict__ z, const float* __restrict__ mask, const unsigned char* __restrict__ packed,
+                      T* __restrict__ xn, T* __restrict__ ab, long long npairs, long long nn, int B, int* status) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* sW = smem;
+  unsigned char* sA = smem + TP_W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TP_W_BYTES + 2 * TP_A_BYTES);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  uint64_t* bar_w = bars;
+  uint64_t* bar_mma = bars + 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long ntiles = (npairs + TILE - 1) / TILE;
+  const float* Pf = reinterpret_cast<const float*>(packed);
+  if ((smem_u32(sA) & 1023u) != 0) {  // the swizzled image needs a 1024-byte aligned base (CTA-uniform)
+    if (tid == 0) atomicCAS(status, 0, (int)DEV_BAD_ALIGN);
+    return;
+  }
+  if (tid == 0) {
+    mbar_init(bar_w, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  if (tid == 0 && (long long)blockIdx.x < ntiles) {
+    mbar_arrive_expect_tx(bar_w, TP_W_BYTES);
+    bulk_g2s(sW, packed + TrimulPacked::img_pg, TP_W_BYTES, bar_w);
+  }
+  const float4 lw = reinterpret_cast<const float4*>(Pf + TrimulPacked::in_w / 4)[lane];
+  const float4 lb = reinterpret_cast<const float4*>(Pf + TrimulPacked::in_b / 4)[lane];
+  auto load_rows = [&](long long tile, float4 (&xv)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const long long p = tile * TILE + warp * 8 + i;
+      xv[i] = p < npairs ? __ldcs(reinterpret_cast<const float4*>(z + p * TM_D) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto ln_tile = [&](int it, long long tile, const float4 (&xv)[8]) {
+    unsigned char* sAi = sA + (it & 1) * TP_A_BYTES;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = warp * 8 + i;
+      const long long p = tile * TILE + r;
+      const float4 v = xv[i];
+      const float mean = tm_warp_sum((v.x + v.y) + (v.z + v.w)) * (1.0f / TM_D);
+      const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+      const float var = tm_warp_sum((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3)) * (1.0f / TM_D);
+      const float rs = rsqrtf(var + LN_EPS);
+      const uint2 pk = make_uint2(H16<T>::pack(d0 * rs * lw.x + lb.x, d1 * rs * lw.y + lb.y),
+                                  H16<T>::pack(d2 * rs * lw.z + lb.z, d3 * rs * lw.w + lb.w));
+      *reinterpret_cast<uint2*>(sAi + sw128_off(r, 4 * lane, TP_A_BYTES / 2)) = pk;
+      if (p < npairs) *reinterpret_cast<uint2*>(xn + p * TM_D + 4 * lane) = pk;
+    }
+  };
+  auto issue_mma = [&](int it) {
+    if (tid == 0) {
+      unsigned char* sAi = sA + (it & 1) * TP_A_BYTES;
+      if (it == 0) mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
+      tc_fence_after();
+      constexpr uint32_t idesc = make_idesc_f16(128, 256, H16<T>::is_bf16, 0, 0);
+#pragma unroll
+      for (int nh = 0; nh < 2; ++nh) {
+#pragma unroll
+        for (int ks = 0; ks < TM_D / 16; ++ks) {
+          const uint64_t ad = smem_desc_sw128(smem_u32(sAi) + (ks / 4) * (TP_A_BYTES / 2) + (ks % 4) * 32);
+          const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * TM_D);
+          umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(bar_mma);
+    }
+  };
+  auto epilogue = [&](int it, long long tile) {
+    const int quad = warp & 3, tt = warp >> 2;
+    const long long p = tile * TILE + quad * 32 + lane;
+    const bool valid = p < npairs;
+    const float m = valid ? (mask ? mask[p] : 1.0f) : 0.0f;
+    const long long bb = valid ? p / nn : 0, pp = valid ? p - bb * nn : 0;
+    mbar_wait(bar_mma, it & 1, status, DEV_TIMEOUT_MMA);
+    __syncwarp();
+    tc_fence_after();
+#pragma unroll 1
+    for (int q4 = 0; q4 < 4; ++q4) {
+      const int c0 = 64 * tt + 16 * q4;  // channel of a | b (0..255)
+      uint32_t pv[16], gv[16];
+      tmem_ld16(tmem_addr(tbase, quad * 32, c0), pv);
+      tmem_ld16(tmem_addr(tbase, quad * 32, 256 + c0), gv);
+      tmem_ld_wait();
+      tmem_regs_ready(pv);
+      tmem_regs_ready(gv);
+      if (valid) {
+        T* dst = ab + ((long long)((c0 >> 7) * B + bb) * TM_D + (c0 & 127)) * nn + pp;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          dst[j * nn] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid(__uint_as_float(gv[j])) * m);
+      }
+    }
+  };
+  float4 xv[8];
+  long long tile = blockIdx.x;
+  if (tile < ntiles) {
+    load_rows(tile, xv);
+    ln_tile(0, tile, xv);
+    if (tile + gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
+    fence_proxy_async_smem();
+    __syncthreads();
+    issue_mma(0);
+  }
+  for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
+    const long long nxt = tile + gridDim.x;
+    if (nxt < ntiles) {
+      ln_tile(it + 1, nxt, xv);  // overlaps the MMA of this tile
+      if (nxt + gridDim.x < ntiles) load_rows(nxt + gridDim.x, xv);
+      fence_proxy_async_smem();
+    }
+    epilogue(it, tile);
+    tc_fence_before();
+    __syncthreads();  // image it + 1 complete; every epilogue done with TMEM
+    tc_fence_after();
+    if (nxt < ntiles) issue_mma(it + 1);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
 // ---- weight packing ------------------------------------------------------------------------------
@@ -190,7 +340,11 @@ __global__ void tm_pack_kernel(const float* in_w, const float* in_b, const float
     // W1 rows: p_in (256) | g_in (256) | g_out (128)
     const float v = r < 2 * TM_D ? p_in[i] : (r < 4 * TM_D ? g_in[i - 2 * TM_D * TM_D] : g_out[i - 4 * TM_D * TM_D]);
     f[TrimulPacked::w1 / 4 + i] = v;
-    if (with16) reinterpret_cast<T*>(packed + TrimulPacked::w1_16)[i] = static_cast<T>(v);
+    if (with16) {
+      reinterpret_cast<T*>(packed + TrimulPacked::w1_16)[i] = static_cast<T>(v);
+      if (r < 4 * TM_D)
+        reinterpret_cast<T*>(packed + TrimulPacked::img_pg)[img_off(r, i % TM_D, TM_D) / 2] = static_cast<T>(v);
+    }
     if (r < TM_D) {
       f[TrimulPacked::p_out / 4 + i] = p_out[i];
       if (with16) reinterpret_cast<T*>(packed + TrimulPacked::p_out_16)[i] = static_cast<T>(p_out[i]);
@@ -256,11 +410,19 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
 
-  *stage = "layernorm_in";
-  tm_ln_in_kernel<T><<<grid_for(P, 8, sms * 16), 256, 0, st>>>(a.z, pf + TrimulPacked::in_w / 4,
-                                                                pf + TrimulPacked::in_b / 4, xn, P);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  cudaError_t e;
+  if constexpr (sizeof(T) == 2) {
+    *stage = "fused projection";
+    cudaFuncSetAttribute(tm_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM);
+    const long long ntiles = (P + TILE - 1) / TILE;
+    tm_proj_tc_kernel<T><<<(int)(ntiles < sms ? ntiles : sms), TP_THREADS, TP_SMEM, st>>>(
+        a.z, a.mask, a.packed, xn, ab, P, nn, a.B, device_status_ptr());
+  } else {
+    *stage = "layernorm_in";
+    tm_ln_in_kernel<T><<<grid_for(P, 8, sms * 16), 256, 0, st>>>(a.z, pf + TrimulPacked::in_w / 4,
+                                                                  pf + TrimulPacked::in_b / 4, xn, P);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   int herr = 0;
   cublasHandle_t hb = blas_handle(&herr);
@@ -274,19 +436,24 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   if (s == CUBLAS_STATUS_SUCCESS) s = cublasSetMathMode(hb, CUBLAS_DEFAULT_MATH);  // fp32 stays fp32 (no TF32)
   const cudaDataType_t tt = cuda_type<T>();
   const float one = 1.0f, zero = 0.0f;
-  // G1 (row-major h [P][640] = xn [P][128] . W1^T; column-major: h^T = W1 . xn^T)
+  // G1, row-major out [P][n] = xn [P][128] . W^T (column-major: out^T = W . xn^T).  16-bit: W = g_out
+  // rows only (a, b come gated from F1); fp32: W = p_in | g_in | g_out, then K2 gates.
+  const int n1 = sizeof(T) == 2 ? TM_D : TM_W1;
+  const T* w1g = sizeof(T) == 2 ? w1 + (size_t)4 * TM_D * TM_D : w1;
   if (s == CUBLAS_STATUS_SUCCESS) {
     *stage = "projection GEMM";
-    s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, TM_W1, (int)P, TM_D, &one, w1, tt, TM_D, xn, tt, TM_D, &zero, h, tt,
-                     TM_W1, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, n1, (int)P, TM_D, &one, w1g, tt, TM_D, xn, tt, TM_D, &zero, h, tt,
+                     n1, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   }
   if (s != CUBLAS_STATUS_SUCCESS) {
     *blas_status = (int)s;
     return cudaErrorUnknown;
   }
-  *stage = "gate";
-  tm_gate_kernel<T><<<(int)((P + TM_GP - 1) / TM_GP), 256, 0, st>>>(h, a.mask, ab, P, nn, a.B);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if constexpr (sizeof(T) == 4) {
+    *stage = "gate";
+    tm_gate_kernel<T><<<(int)((P + TM_GP - 1) / TM_GP), 256, 0, st>>>(h, a.mask, ab, P, nn, a.B);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   // G2, per (batch, channel), row-major N x N matrices (column-major views are their transposes):
   //   outgoing o = a . b^T   ->  o^T = b . a^T   (op(b) = T on b^T, op(a^T) = N)
   //   incoming o = a^T . b   ->  o^T = b^T . a   (op(b^T) = N, op(a) = T on a^T)
@@ -313,7 +480,9 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
     return cudaErrorUnknown;
   }
   *stage = "output gate";
-  tm_out_kernel<T><<<grid_for(P * 32, 256, sms * 16), 256, 0, st>>>(a.z, y, h, a.out, P * 32, a.add_residual);
+  const T* gout = sizeof(T) == 2 ? h : h + 4 * TM_D;  // [P][128] g_out, or the g_out columns of h [P][640]
+  tm_out_kernel<T><<<grid_for(P * 32, 256, sms * 16), 256, 0, st>>>(a.z, y, gout, n1, a.out, P * 32,
+                                                                     a.add_residual);
   return cudaGetLastError();
 }
 
