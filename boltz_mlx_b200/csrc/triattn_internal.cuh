@@ -97,8 +97,8 @@ struct Workspace {
 // ---- triangle multiplication (outgoing / incoming edges) -----------------------------------------
 // packed weights: fp32 section: in_w, in_b, out_w, out_b [128 each]; W1 = p_in | g_in | g_out
 // [640][128]; p_out [128][128].  16-bit section (16-bit modes): W1 and p_out in the layer's type,
-// row-major (cuBLAS operands), and the p_in | g_in rows (512 x 128) once more as a K-major no-swizzle
-// UMMA operand image (img_off) for the fused projection kernel.
+// row-major (cuBLAS operands), and the p_in | g_in rows (512 x 128) and p_out (128 x 128) once more as
+// K-major no-swizzle UMMA operand images (img_off) for the fused projection and tail kernels.
 constexpr int TM_D = 128;
 constexpr int TM_W1 = 5 * TM_D;  // 640 = p_in (256) | g_in (256) | g_out (128)
 struct TrimulPacked {
@@ -109,7 +109,8 @@ struct TrimulPacked {
   static constexpr size_t w1_16 = align_up(f32_end, 256);
   static constexpr size_t p_out_16 = w1_16 + (size_t)TM_W1 * TM_D * 2;
   static constexpr size_t img_pg = align_up(p_out_16 + (size_t)TM_D * TM_D * 2, 1024);
-  static constexpr size_t end16 = img_pg + (size_t)4 * TM_D * TM_D * 2;
+  static constexpr size_t img_po = img_pg + (size_t)4 * TM_D * TM_D * 2;  // p_out as a 128 x 128 image
+  static constexpr size_t end16 = img_po + (size_t)TM_D * TM_D * 2;
   static constexpr size_t bytes(int dtype) { return dtype == DT_F32 ? align_up(f32_end, 256) : align_up(end16, 256); }
 };
 // workspace of one call over P = B*N*N pairs (es = element size of the layer's type):

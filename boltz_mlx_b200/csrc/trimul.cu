@@ -328,6 +328,141 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
+// ---- T1 (16-bit modes): the tail in one kernel: norm_out + p_out MMA + output gate + residual ------
+// Tile = 128 consecutive pairs, one per CTA, 256 threads, three CTAs per SM.
+//   norm_out: thread (pair r = tid % 128, half = tid / 128) holds channels 64 half.. of o for its pair
+//     in registers (a warp's loads are 128-byte runs: 32 consecutive pairs of one channel row); the
+//     two halves' sums meet in shared memory; two-pass fp32 statistics as the reference; the 16-bit
+//     result goes into a K-major operand image.
+//   MMA: D[128 x 128] = norm_out(o) . p_out^T (TMEM 128 columns).
+//   epilogue: the accumulator is staged through shared memory (rows of 132 floats, over the operand
+//     images), then warp w streams rows 16w..16w+15 whole: out = z + y * sigmoid(g_out).
+constexpr int TT_THREADS = 256;
+constexpr int TT_STAGE_LD = TM_D + 4;
+constexpr int TT_SMEM_BODY = TILE * TT_STAGE_LD * 4;  // 67584 B, covers the two 32 KB operand images
+constexpr int TT_SMEM = TT_SMEM_BODY + 2 * 2 * TILE * 4 + 64;
+
+template <typename T>
+__global__ void __launch_bounds__(TT_THREADS, 3)
+    tm_tail_tc_kernel(const float* __restrict__ o, const unsigned char* __restrict__ packed, const T* __restrict__ gout,
+                      const float* z, float* out, long long npairs, long long nn, int add_residual, int* status) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* sA = smem;
+  unsigned char* sW = smem + 32768;
+  float* stage = reinterpret_cast<float*>(smem);  // after the MMA
+  float* red = reinterpret_cast<float*>(smem + TT_SMEM_BODY);  // [2 stats][2 halves][128 pairs]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TT_SMEM_BODY + 2 * 2 * TILE * 4);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long p0 = (long long)blockIdx.x * TILE;
+  const float* Pf = reinterpret_cast<const float*>(packed);
+  if (tid == 0) {
+    mbar_init(bars + 0, 1);
+    mbar_init(bars + 1, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tslot, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bars + 0, 32768);
+    bulk_g2s(sW, packed + TrimulPacked::img_po, 32768, bars + 0);
+  }
+  // ---- norm_out of pair r over channels 64 half .. 64 half + 63 ----
+  {
+    const int r = tid & (TILE - 1), half = tid >> 7;
+    const long long p = p0 + r;
+    const bool valid = p < npairs;
+    const long long bb = valid ? p / nn : 0, pp = valid ? p - bb * nn : 0;
+    const float* src = o + (bb * TM_D + 64 * half) * nn + pp;
+    float v[64];
+#pragma unroll
+    for (int d = 0; d < 64; ++d) v[d] = valid ? __ldcs(src + d * nn) : 0.0f;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int d = 0; d < 64; d += 2) { s0 += v[d]; s1 += v[d + 1]; }
+    red[half * TILE + r] = s0 + s1;
+    __syncthreads();
+    const float mean = (red[r] + red[TILE + r]) * (1.0f / TM_D);
+    float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+    for (int d = 0; d < 64; d += 2) {
+      const float e0 = v[d] - mean, e1 = v[d + 1] - mean;
+      q0 += e0 * e0;
+      q1 += e1 * e1;
+    }
+    red[2 * TILE + half * TILE + r] = q0 + q1;
+    __syncthreads();
+    const float var = (red[2 * TILE + r] + red[3 * TILE + r]) * (1.0f / TM_D);
+    const float rs = rsqrtf(var + LN_EPS);
+    const float* lw = Pf + TrimulPacked::out_w / 4 + 64 * half;
+    const float* lb = Pf + TrimulPacked::out_b / 4 + 64 * half;
+#pragma unroll
+    for (int d = 0; d < 64; d += 8) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        w4[e] = H16<T>::pack((v[d + 2 * e] - mean) * rs * __ldg(lw + d + 2 * e) + __ldg(lb + d + 2 * e),
+                             (v[d + 2 * e + 1] - mean) * rs * __ldg(lw + d + 2 * e + 1) + __ldg(lb + d + 2 * e + 1));
+      *reinterpret_cast<uint4*>(sA + img_off(r, 64 * half + d, TM_D)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    mbar_wait(bars + 0, 0, status, DEV_TIMEOUT_TMA);
+    tc_fence_after();
+    constexpr uint32_t idesc = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
+#pragma unroll
+    for (int ks = 0; ks < TM_D / 16; ++ks) {
+      const uint64_t ad = smem_desc_noswizzle(smem_u32(sA) + ks * 256, 128, 16 * TM_D);
+      const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + ks * 256, 128, 16 * TM_D);
+      umma_ss(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
+    }
+    umma_commit(bars + 1);
+  }
+  mbar_wait(bars + 1, 0, status, DEV_TIMEOUT_MMA);  // MMA done: the operand images are free for staging
+  __syncwarp();
+  tc_fence_after();
+  {
+    const int quad = warp & 3, part = warp >> 2;
+    float* srow = stage + (quad * 32 + lane) * TT_STAGE_LD + 64 * part;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      uint32_t acc[32];
+      tmem_ld32(tmem_addr(tbase, quad * 32, 64 * part + 32 * h2), acc);
+      tmem_ld_wait();
+      tmem_regs_ready(acc);
+#pragma unroll
+      for (int d = 0; d < 32; d += 4)
+        *reinterpret_cast<float4*>(srow + 32 * h2 + d) =
+            make_float4(__uint_as_float(acc[d]), __uint_as_float(acc[d + 1]), __uint_as_float(acc[d + 2]),
+                        __uint_as_float(acc[d + 3]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // ---- rows 16 warp .. 16 warp + 15: out = z + y * sigmoid(g_out), lane = channels 4 lane.. ----
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int r = 16 * warp + i;
+    const long long p = p0 + r;
+    if (p >= npairs) break;  // warp-uniform
+    const float4 y = *reinterpret_cast<const float4*>(stage + r * TT_STAGE_LD + 4 * lane);
+    const float4 g = Ew<T>::ld4(gout + p * TM_D + 4 * lane);
+    float4 res = make_float4(y.x * tm_sigmoid(g.x), y.y * tm_sigmoid(g.y), y.z * tm_sigmoid(g.z), y.w * tm_sigmoid(g.w));
+    if (add_residual) {
+      const float4 zv = reinterpret_cast<const float4*>(z + p * TM_D)[lane];  // out may alias z
+      res.x += zv.x; res.y += zv.y; res.z += zv.z; res.w += zv.w;
+    }
+    reinterpret_cast<float4*>(out + p * TM_D)[lane] = res;
+  }
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 128);
+}
+
 // ---- weight packing ------------------------------------------------------------------------------
 template <typename T>
 __global__ void tm_pack_kernel(const float* in_w, const float* in_b, const float* p_in, const float* g_in,
@@ -344,6 +479,8 @@ __global__ void tm_pack_kernel(const float* in_w, const float* in_b, const float
       reinterpret_cast<T*>(packed + TrimulPacked::w1_16)[i] = static_cast<T>(v);
       if (r < 4 * TM_D)
         reinterpret_cast<T*>(packed + TrimulPacked::img_pg)[img_off(r, i % TM_D, TM_D) / 2] = static_cast<T>(v);
+      if (r < TM_D)
+        reinterpret_cast<T*>(packed + TrimulPacked::img_po)[img_off(r, i % TM_D, TM_D) / 2] = static_cast<T>(p_out[i]);
     }
     if (r < TM_D) {
       f[TrimulPacked::p_out / 4 + i] = p_out[i];
@@ -467,6 +604,14 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
     *blas_status = (int)s;
     return cudaErrorUnknown;
   }
+  const T* gout = sizeof(T) == 2 ? h : h + 4 * TM_D;  // [P][128] g_out, or the g_out columns of h [P][640]
+  if constexpr (sizeof(T) == 2) {
+    *stage = "tail";
+    cudaFuncSetAttribute(tm_tail_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+    tm_tail_tc_kernel<T><<<(int)((P + TILE - 1) / TILE), TT_THREADS, TT_SMEM, st>>>(
+        o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, device_status_ptr());
+    return cudaGetLastError();
+  }
   *stage = "layernorm_out";
   tm_ln_out_kernel<T><<<(int)((P + TM_LP - 1) / TM_LP), 256, 0, st>>>(o, pf + TrimulPacked::out_w / 4,
                                                                         pf + TrimulPacked::out_b / 4, xn, P, nn);
@@ -480,7 +625,6 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
     return cudaErrorUnknown;
   }
   *stage = "output gate";
-  const T* gout = sizeof(T) == 2 ? h : h + 4 * TM_D;  // [P][128] g_out, or the g_out columns of h [P][640]
   tm_out_kernel<T><<<grid_for(P * 32, 256, sms * 16), 256, 0, st>>>(a.z, y, gout, n1, a.out, P * 32,
                                                                      a.add_residual);
   return cudaGetLastError();
