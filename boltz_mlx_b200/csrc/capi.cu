@@ -494,9 +494,9 @@ int triattn_trimul_pack_weights(const float* in_w, const float* in_b, const floa
                 "trimul_pack_weights");
 }
 
-int triattn_trimul_forward(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
-                           int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
-                           void* stream) {
+static int trimul_call(const float* z, const float* mask, const void* packed, int B, int N, int outgoing, int dtype,
+                       int add_residual, float* out, const float* ln_next_w, const float* ln_next_b, void* ln_out,
+                       void* workspace, size_t workspace_bytes, void* stream) {
   if (int r = check_dims(B, N, dtype)) return r;
   if ((long long)B * N * N > 2147483647LL) return fail(TRIATTN_EUNSUPPORTED, "B*N*N above 2^31 pairs");
   if (!z || !aligned(z, 16)) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
@@ -510,12 +510,31 @@ int triattn_trimul_forward(const float* z, const float* mask, const void* packed
   a.z = z; a.mask = mask; a.packed = static_cast<const unsigned char*>(packed);
   a.B = B; a.N = N; a.outgoing = outgoing ? 1 : 0; a.dtype = dtype; a.add_residual = add_residual ? 1 : 0;
   a.out = out; a.ws = static_cast<unsigned char*>(workspace);
+  a.ln_next_w = ln_next_w; a.ln_next_b = ln_next_b; a.ln_out = ln_out;
   int blas = 0;
   const char* stage = "";
   const cudaError_t e = launch_trimul(a, static_cast<cudaStream_t>(stream), &blas, &stage);
   if (blas) return fail(TRIATTN_ECUDA, "trimul %s: cuBLAS status %d", stage, blas);
   if (e != cudaSuccess) return fail(TRIATTN_ECUDA, "trimul %s: %s", stage, cudaGetErrorString(e));
   return TRIATTN_OK;
+}
+
+int triattn_trimul_forward(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
+                           int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  return trimul_call(z, mask, packed, B, N, outgoing, dtype, add_residual, out, nullptr, nullptr, nullptr, workspace,
+                     workspace_bytes, stream);
+}
+
+int triattn_trimul_forward_addln(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
+                                 int dtype, float* out, const float* ln_next_w, const float* ln_next_b, void* ln_out,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype == DT_F32) return fail(TRIATTN_EUNSUPPORTED, "trimul addln belongs to the 16-bit path");
+  if (!ln_out || !aligned(ln_out, 16) || !ln_next_w || !ln_next_b || !aligned(ln_next_w, 16) ||
+      !aligned(ln_next_b, 16))
+    return fail(TRIATTN_EINVAL, "ln_out needs 16-byte aligned ln_out, ln_next_w and ln_next_b");
+  return trimul_call(z, mask, packed, B, N, outgoing, dtype, 1, out, ln_next_w, ln_next_b, ln_out, workspace,
+                     workspace_bytes, stream);
 }
 
 int triattn_forward_chunked(const float* z, const float* mask, const void* packed, int B, int N, int starting,

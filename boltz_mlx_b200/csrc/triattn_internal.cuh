@@ -141,6 +141,8 @@ struct TrimulArgs {
   const float* z; const float* mask; const unsigned char* packed;
   int B, N, outgoing, dtype, add_residual;
   float* out; unsigned char* ws;
+  // optional (16-bit modes): the next module's LayerNorm of out, written in the layer's type
+  const float* ln_next_w; const float* ln_next_b; void* ln_out;
 };
 
 // Byte offset of tri-bias element (q, k) of head h, batch b on the 16-bit path.

@@ -342,10 +342,12 @@ constexpr int TT_STAGE_LD = TM_D + 4;
 constexpr int TT_SMEM_BODY = TILE * TT_STAGE_LD * 4;  // 67584 B, covers the two 32 KB operand images
 constexpr int TT_SMEM = TT_SMEM_BODY + 2 * 2 * TILE * 4 + 64;
 
-template <typename T>
+template <typename T, bool LN_NEXT>
 __global__ void __launch_bounds__(TT_THREADS, 3)
     tm_tail_tc_kernel(const float* __restrict__ o, const unsigned char* __restrict__ packed, const T* __restrict__ gout,
-                      const float* z, float* out, long long npairs, long long nn, int add_residual, int* status) {
+                      const float* z, float* out, long long npairs, long long nn, int add_residual,
+                      const float* __restrict__ ln_w, const float* __restrict__ ln_b, T* __restrict__ ln_out,
+                      int* status) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
   unsigned char* sW = smem + 32768;
@@ -444,7 +446,13 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
   }
   tc_fence_before();
   __syncthreads();
-  // ---- rows 16 warp .. 16 warp + 15: out = z + y * sigmoid(g_out), lane = channels 4 lane.. ----
+  // ---- rows 16 warp .. 16 warp + 15: out = z + y * sigmoid(g_out), lane = channels 4 lane.. (and
+  //      the next module's LayerNorm of the new row, two-pass fp32 statistics, one 16-bit rounding) ----
+  float4 nw = make_float4(0.f, 0.f, 0.f, 0.f), nb = nw;
+  if constexpr (LN_NEXT) {
+    nw = reinterpret_cast<const float4*>(ln_w)[lane];
+    nb = reinterpret_cast<const float4*>(ln_b)[lane];
+  }
 #pragma unroll 4
   for (int i = 0; i < 16; ++i) {
     const int r = 16 * warp + i;
@@ -458,6 +466,14 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
       res.x += zv.x; res.y += zv.y; res.z += zv.z; res.w += zv.w;
     }
     reinterpret_cast<float4*>(out + p * TM_D)[lane] = res;
+    if constexpr (LN_NEXT) {
+      const float mean = tm_warp_sum((res.x + res.y) + (res.z + res.w)) * (1.0f / TM_D);
+      const float d0 = res.x - mean, d1 = res.y - mean, d2 = res.z - mean, d3 = res.w - mean;
+      const float var = tm_warp_sum((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3)) * (1.0f / TM_D);
+      const float rs = rsqrtf(var + LN_EPS);
+      Ew<T>::st4(ln_out + p * TM_D + 4 * lane, make_float4(d0 * rs * nw.x + nb.x, d1 * rs * nw.y + nb.y,
+                                                         d2 * rs * nw.z + nb.z, d3 * rs * nw.w + nb.w));
+    }
   }
   __syncthreads();
   if (warp == 0) tmem_dealloc(tbase, 128);
@@ -607,9 +623,18 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   const T* gout = sizeof(T) == 2 ? h : h + 4 * TM_D;  // [P][128] g_out, or the g_out columns of h [P][640]
   if constexpr (sizeof(T) == 2) {
     *stage = "tail";
-    cudaFuncSetAttribute(tm_tail_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
-    tm_tail_tc_kernel<T><<<(int)((P + TILE - 1) / TILE), TT_THREADS, TT_SMEM, st>>>(
-        o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, device_status_ptr());
+    const int grid = (int)((P + TILE - 1) / TILE);
+    if (a.ln_out) {
+      cudaFuncSetAttribute(tm_tail_tc_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+      tm_tail_tc_kernel<T, true><<<grid, TT_THREADS, TT_SMEM, st>>>(
+          o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, a.ln_next_w, a.ln_next_b,
+          reinterpret_cast<T*>(a.ln_out), device_status_ptr());
+    } else {
+      cudaFuncSetAttribute(tm_tail_tc_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+      tm_tail_tc_kernel<T, false><<<grid, TT_THREADS, TT_SMEM, st>>>(o, a.packed, gout, a.z, a.out, P, nn,
+                                                                      a.add_residual, nullptr, nullptr, nullptr,
+                                                                      device_status_ptr());
+    }
     return cudaGetLastError();
   }
   *stage = "layernorm_out";

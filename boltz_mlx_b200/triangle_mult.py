@@ -99,6 +99,43 @@ class _TriangleMultiplication(nn.Module):
         out = zc if (inplace and zc is z and z.dtype == torch.float32) else None
         return self._run(zc, mask, True, out)
 
+    def f16_addln(self, z: torch.Tensor, mask: Optional[torch.Tensor], xn: Optional[torch.Tensor], ln_next,
+                  w_tb: Optional[torch.Tensor] = None):
+        """(z + self(z), ln_next(z + self(z)) 16-bit[, next tri bias]) as the reference's f16_addln
+        (triangular_mult.py:93-115): the output gate, the residual add and the next module's LayerNorm in
+        the tail kernel.  16-bit precisions only.  `xn` (norm_in(z), precomputed) is accepted and
+        recomputed from z.  `w_tb` [H, 128]: also return the next triangle attention's tri bias
+        LN_out . w_tb^T as [B, H, N, N]."""
+        del xn
+        if not z.is_cuda:
+            raise RuntimeError("TriangleMultiplication (B200) needs CUDA tensors; there is no CPU path")
+        dtype = _lib.dtype_code(self.precision)
+        if dtype == _lib.F32:
+            raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED, "f16_addln belongs to the 16-bit path (fp16 or bf16)")
+        if z.dim() != 4 or z.shape[1] != z.shape[2] or z.shape[3] != self.dim or z.dtype != torch.float32:
+            raise ValueError(f"z must be fp32 [B, N, N, {self.dim}], got {tuple(z.shape)} {z.dtype}")
+        zc = z.contiguous()
+        B, N = zc.shape[0], zc.shape[1]
+        m = None
+        if mask is not None:
+            if tuple(mask.shape) != (B, N, N):
+                raise ValueError(f"mask must be [B, N, N] = {(B, N, N)}, got {tuple(mask.shape)}")
+            m = mask.to(device=zc.device, dtype=torch.float32).contiguous()
+        t16 = torch.bfloat16 if dtype == _lib.BF16 else torch.float16
+        lw = ln_next.weight.detach().to(device=zc.device, dtype=torch.float32).contiguous()
+        lb = ln_next.bias.detach().to(device=zc.device, dtype=torch.float32).contiguous()
+        out = torch.empty_like(zc)
+        ln_out = torch.empty(zc.shape, dtype=t16, device=zc.device)
+        packed = self.packed_weights(dtype)
+        ws = self._ws.get(_lib.lib().triattn_trimul_workspace_bytes(B, N, dtype), zc.device)
+        _lib.check(_lib.lib().triattn_trimul_forward_addln(
+            zc.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N, int(self.outgoing), dtype, out.data_ptr(),
+            lw.data_ptr(), lb.data_ptr(), ln_out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(zc.device)))
+        if w_tb is None:
+            return out, ln_out
+        w = w_tb.to(device=ln_out.device, dtype=ln_out.dtype)
+        return out, ln_out, (ln_out @ w.t()).permute(0, 3, 1, 2).contiguous()
+
 
 class TriangleMultiplicationOutgoing(_TriangleMultiplication):
     """o[i,j] = sum_k a[i,k] b[j,k] (triangular_mult.py:173-174)."""

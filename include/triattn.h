@@ -251,6 +251,14 @@ TRIATTN_API size_t triattn_trimul_workspace_bytes(int B, int N, int dtype);
 TRIATTN_API int triattn_trimul_forward(const float* z, const float* mask, const void* packed, int B, int N,
                                        int outgoing, int dtype, int add_residual, float* out, void* workspace,
                                        size_t workspace_bytes, void* stream);
+/* out = z + TriangleMultiplication(z) and ln_out = LN_next(out) in the layer's 16-bit type, from one
+ * tail kernel <- the reference's f16_addln (triangular_mult.py:93-115, kernels_nax3.trimul_tail_addln):
+ * the next module (a triangle attention, whose `xn` input this is) skips its LayerNorm.  16-bit
+ * dtypes only; ln_out [B][N][N][128] in z's orientation; ln_next_w / ln_next_b fp32 [128]. */
+TRIATTN_API int triattn_trimul_forward_addln(const float* z, const float* mask, const void* packed, int B, int N,
+                                             int outgoing, int dtype, float* out, const float* ln_next_w,
+                                             const float* ln_next_b, void* ln_out, void* workspace,
+                                             size_t workspace_bytes, void* stream);
 
 /* ---- allocation-free layer ----------------------------------------------------------------
  * No counterpart in the reference.  triattn_forward without a workspace argument, for callers that

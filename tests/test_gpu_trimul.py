@@ -96,3 +96,31 @@ def test_trimul_bench_size_bf16():
 def test_trimul_parameter_names_match_reference():
     mod = TriangleMultiplicationOutgoing(128)
     assert sorted(n for n, _ in mod.named_parameters()) == sorted(REF_NAMES.values())
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+def test_trimul_f16_addln_feeds_the_next_layernorm(precision):
+    """f16_addln: z + y equals forward_residual bit for bit, and ln_out equals the next module's
+    LayerNorm of it (fp32 statistics, one 16-bit rounding); the next tri bias from w_tb."""
+    z, m = _inputs(1, 70, 17)
+    p = make_params(14)
+    ln = torch.nn.LayerNorm(128, eps=1e-5).cuda()
+    with torch.no_grad():
+        ln.weight.copy_(1.0 + 0.1 * torch.randn(128))
+        ln.bias.copy_(0.1 * torch.randn(128))
+    w_tb = torch.randn(4, 128).cuda() / 128 ** 0.5
+    t16 = torch.bfloat16 if precision == "bf16" else torch.float16
+    for outgoing in (True, False):
+        mod = _module(p, outgoing, precision)
+        zc, mc = z.cuda(), m.cuda()
+        z_new, ln_out, tb = mod.f16_addln(zc, mc, None, ln, w_tb=w_tb)
+        assert torch.equal(z_new, mod.forward_residual(zc, mc))
+        ref = torch.nn.functional.layer_norm(z_new, (128,), ln.weight, ln.bias, 1e-5)
+        assert ln_out.dtype == t16
+        d = (ln_out.float() - ref).abs()
+        tol = 1e-2 if precision == "bf16" else 2e-3
+        assert float(d.max()) <= tol * max(1.0, float(ref.abs().max())), float(d.max())
+        assert tb.shape == (1, 4, 70, 70)
+        assert torch.allclose(tb.float(), (ln_out.float() @ w_tb.t()).permute(0, 3, 1, 2), rtol=2e-2, atol=2e-2)
+    with pytest.raises(_lib.TriAttnUnsupported):
+        _module(p, True, "fp32").f16_addln(z.cuda(), m.cuda(), None, ln)
