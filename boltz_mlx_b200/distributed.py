@@ -539,7 +539,7 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
                         "ms_per_step": float(e2e), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
                         "d2h_bytes_per_step": oh.numel() * 4 * ws_n,
                         "pipelined": "input copy, pair and output copy of consecutive steps overlap (2 device slots)"},
-                "gpu_launches": args.steps * 2 * (5 if exchange == "peer" else 4),
+                "gpu_launches": args.steps * 2 * (7 if exchange == "peer" else 4),
                 "device_status": int(status),
                 "clocks": clk.summary(),
             }
