@@ -169,3 +169,34 @@ def decode_core_images(buf, w: Workspace):
     raw = buf[w.off_core:w.off_core + n].view(torch.float16).view(w.B, w.R, w.NT, 16384)
     idx = torch.from_numpy(img_offsets(TILE, C_IN) // 2).to(buf.device)
     return raw[..., idx].float().reshape(w.B, w.R, w.Np, C_IN)
+
+
+# ---- triangle multiplication (csrc/triattn_internal.cuh: TrimulPacked, TrimulWorkspace) -------------
+TM_D, TM_W1 = 128, 640
+TRIMUL_BLAS_BYTES = 32 << 20
+
+
+def trimul_packed_bytes(dtype: int) -> int:
+    """Packed tri-mult weights: fp32 LayerNorm vectors (2 KB), W1 = p_in | g_in | g_out [640][128] and
+    p_out [128][128] in fp32; 16-bit modes add both row-major in the layer's type, then the p_in | g_in
+    (512 x 128) and p_out (128 x 128) operand images (1024-byte aligned)."""
+    f32_end = 2048 + TM_W1 * TM_D * 4 + TM_D * TM_D * 4
+    if dtype == F32:
+        return align(f32_end)
+    w1_16 = align(f32_end)
+    p_out_16 = w1_16 + TM_W1 * TM_D * 2
+    img_pg = align(p_out_16 + TM_D * TM_D * 2, 1024)
+    img_po = img_pg + 4 * TM_D * TM_D * 2
+    return align(img_po + TM_D * TM_D * 2)
+
+
+def trimul_workspace_bytes(B: int, N: int, dtype: int) -> int:
+    """Tri-mult workspace: xn [P][128], h (fp32: [P][640]; 16-bit: g_out [P][128]), a|b channel-major
+    (or p_out's fp32 output, whichever is larger), o fp32 [B][128][N][N], 32 MiB cuBLAS scratch."""
+    P = B * N * N
+    es = 4 if dtype == F32 else 2
+    o = align(P * TM_D * es)
+    o = align(o + P * (TM_W1 if dtype == F32 else TM_D) * es)
+    o = align(o + max(2 * P * TM_D * es, P * TM_D * 4))
+    o = align(o + P * TM_D * 4)
+    return align(o + TRIMUL_BLAS_BYTES)

@@ -104,3 +104,24 @@ def test_module_refuses_cpu_tensors_and_other_geometries():
     names = {n for n, _ in m.named_parameters()}
     assert names == {"layer_norm.weight", "layer_norm.bias", "linear.weight", "mha.linear_q.weight",
                      "mha.linear_k.weight", "mha.linear_v.weight", "mha.linear_o.weight", "mha.linear_g.weight"}
+
+
+@pytest.mark.parametrize("dtype", [_lib.F32, _lib.F16, _lib.BF16])
+@pytest.mark.parametrize("B,N", [(1, 1), (2, 9), (1, 128), (1, 1024), (3, 37)])
+def test_trimul_sizes_match_library(L, dtype, B, N):
+    assert L.triattn_trimul_workspace_bytes(B, N, dtype) == layout.trimul_workspace_bytes(B, N, dtype)
+    assert L.triattn_trimul_packed_bytes(dtype) == layout.trimul_packed_bytes(dtype)
+
+
+def test_trimul_host_validation(L):
+    ws = 256 * 4096
+    assert L.triattn_trimul_forward(4096, None, 256 * 16, 1, 0, 1, _lib.BF16, 1, 4096, ws, 1 << 34, None) == _lib.EINVAL
+    assert L.triattn_trimul_forward(4096 + 4, None, 256 * 16, 1, 8, 1, _lib.BF16, 1, 4096, ws, 1 << 34, None) == _lib.EINVAL
+    assert L.triattn_trimul_forward(4096, None, 256 * 16, 1, 8, 1, _lib.BF16, 1, 4096, ws, 16, None) == _lib.ENOSPACE
+    assert L.triattn_trimul_forward(4096, None, 256 * 16, 1, 8, 1, 9, 1, 4096, ws, 1 << 34, None) == _lib.EUNSUPPORTED
+    # addln: 16-bit only, and its LayerNorm pointers are checked
+    assert L.triattn_trimul_forward_addln(4096, None, 256 * 16, 1, 8, 1, _lib.F32, 4096, 4096, 4096, 4096, ws,
+                                          1 << 34, None) == _lib.EUNSUPPORTED
+    assert L.triattn_trimul_forward_addln(4096, None, 256 * 16, 1, 8, 1, _lib.BF16, 4096, None, 4096, 4096, ws,
+                                          1 << 34, None) == _lib.EINVAL
+    assert L.triattn_trimul_pack_weights(*([None] * 8), _lib.BF16, 4096, 1 << 20, None) == _lib.EINVAL

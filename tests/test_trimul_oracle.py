@@ -2,11 +2,28 @@
 einsum formulation, on the reference tests' shapes (tiny and ragged N, B = 2, masked rows and
 columns), both edge directions; channel blocking does not change the result."""
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
 
-from oracle.trimul_ref import make_params, trimul_np64, trimul_ref
+from oracle.trimul_ref import PARAM_SHAPES, make_params, trimul_np64, trimul_ref
+
+GOLDEN = Path(__file__).parent / "golden" / "trimul_golden.npz"
+
+
+def golden_cases():
+    d = np.load(GOLDEN)
+    return d, sorted({k[:-5] for k in d.files if k.endswith("_meta")})
+
+
+def golden_case(d, name):
+    B, N, pid = (int(x) for x in d[f"{name}_meta"])
+    z = torch.from_numpy(d[f"{name}_z"].astype(np.float32))
+    m = torch.from_numpy(d[f"{name}_mask"].astype(np.float32)) if f"{name}_mask" in d.files else None
+    p = {k: torch.from_numpy(d[f"p{pid}_{k}"]) for k in PARAM_SHAPES}
+    return z, m, p
 
 
 def _inputs(B, N, seed):
@@ -48,3 +65,23 @@ def test_incoming_is_outgoing_on_the_transpose():
     yin = trimul_ref(z, m, p, outgoing=False, dtype=torch.float64)
     yout_t = trimul_ref(z.transpose(1, 2), m.transpose(1, 2), p, outgoing=True, dtype=torch.float64)
     assert torch.allclose(yin, yout_t, rtol=1e-12, atol=1e-12)
+
+
+def test_golden_fixtures_reproduce():
+    """The committed fixtures (tests/golden/make_trimul_golden.py) are the oracle's float64 output stored
+    in float32: the float64 oracle reproduces them to that rounding, the independent einsum form agrees,
+    and the fp32 oracle stays within 1e-5 of them (the fp32 bar)."""
+    d, names = golden_cases()
+    assert len(names) == 5
+    for name in names:
+        z, m, p = golden_case(d, name)
+        for outgoing, tag in ((True, "out"), (False, "in")):
+            want = d[f"{name}_y_{tag}"].astype(np.float64)  # stored in float32
+            got = trimul_ref(z.double(), None if m is None else m.double(), p, outgoing=outgoing,
+                             dtype=torch.float64).numpy()
+            np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-6)
+            alt = trimul_np64(z.numpy(), None if m is None else m.numpy(), {k: v.numpy() for k, v in p.items()},
+                              outgoing=outgoing)
+            np.testing.assert_allclose(alt, want, rtol=1e-6, atol=1e-6)
+            f32 = trimul_ref(z, m, p, outgoing=outgoing).numpy()
+            assert np.abs(f32 - want).max() <= 1e-5 * max(1.0, np.abs(want).max()), name
