@@ -125,6 +125,10 @@ class PeerSpace:
     ptrs[q] is rank q's buffer as seen from this process (ptrs[rank] = the own buffer)."""
 
     def __init__(self, nbytes: int, device: torch.device, group=None):
+        with torch.cuda.device(device):  # the allocation, the IPC mappings and the all-gather on `device`
+            self._setup(nbytes, device, group)
+
+    def _setup(self, nbytes: int, device: torch.device, group) -> None:
         L = _lib.lib()
         self.group, self.device, self.nbytes = group, device, nbytes
         self.P, self.rank = dist.get_world_size(group), dist.get_rank(group)
@@ -161,13 +165,14 @@ class PeerSpace:
         if self.own is None:
             return
         L = _lib.lib()
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        for p in self._opened:
-            _lib.check(L.triattn_ipc_close(p))
-        self._opened = []
-        dist.barrier(group=self.group)
-        _lib.check(L.triattn_peer_free(self.own))
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            for p in self._opened:
+                _lib.check(L.triattn_ipc_close(p))
+            self._opened = []
+            dist.barrier(group=self.group)
+            _lib.check(L.triattn_peer_free(self.own))
         self.own = None
 
 
