@@ -110,6 +110,19 @@ def cols_to_blocks(zt: torch.Tensor, z_blk: torch.Tensor, group=None) -> None:
     dist.all_to_all_single(z_blk, zt.view(P, R, R, Cc), group=group)
 
 
+def all_ranks_ok(ok: bool, group=None, device: Optional[torch.device] = None) -> bool:
+    """True on every rank iff `ok` is True on every rank of the group (one all-reduce, MIN): a setup
+    step that can fail on some ranks only is then accepted or rejected by all of them together."""
+    dev = device if device is not None and dist.get_backend(group) == "nccl" else torch.device("cpu")
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(t.item()))
+
+
+class PeerUnavailable(RuntimeError):
+    """Some rank could not map another rank's buffer (no peer access between those GPUs)."""
+
+
 class _DeviceArray:
     """A raw device allocation described by __cuda_array_interface__ (torch.as_tensor wraps it
     without a copy; the wrapper keeps `owner` alive)."""
@@ -140,14 +153,21 @@ class PeerSpace:
         handles = [None] * self.P
         dist.all_gather_object(handles, h.raw, group=group)
         self.ptrs, self._opened = [], []
+        err = None
         for q, hq in enumerate(handles):
             if q == self.rank:
                 self.ptrs.append(self.own)
                 continue
             p = ctypes.c_void_p()
-            _lib.check(L.triattn_ipc_open(ctypes.create_string_buffer(hq, _lib.IPC_HANDLE_BYTES), ctypes.byref(p)))
+            rc = L.triattn_ipc_open(ctypes.create_string_buffer(hq, _lib.IPC_HANDLE_BYTES), ctypes.byref(p))
+            if rc != _lib.OK:
+                err = f"rank {self.rank} cannot map rank {q}'s buffer: {(L.triattn_last_error_string() or b'').decode()}"
+                break
             self.ptrs.append(p.value)
             self._opened.append(p.value)
+        if not all_ranks_ok(err is None, group, device):
+            self.close()  # every rank unmaps what it mapped and frees its own buffer
+            raise PeerUnavailable(err or "another rank could not map a peer buffer")
 
     def tensor(self, offset: int, shape, dtype=torch.float32) -> torch.Tensor:
         """A view of this rank's own buffer at byte `offset`."""
@@ -231,7 +251,12 @@ class ShardedPair:
         self.peer = None
         if exchange == "peer":
             self.lay = lay = peer_layout(N, self.P, self.w.total)
-            self.peer = PeerSpace(lay["total"], device, group)
+            try:
+                self.peer = PeerSpace(lay["total"], device, group)
+            except PeerUnavailable as e:  # all ranks together: the all-to-all exchange instead
+                print(f"ShardedPair: peer exchange unavailable ({e}); using NCCL all-to-alls", flush=True)
+                exchange = self.exchange = "nccl"
+        if exchange == "peer":
             self.zc = self.peer.tensor(lay["zc"], (N, self.R, C_IN))
             self.zb = self.peer.tensor(lay["zb"], (self.P, self.R, self.R, C_IN))
             self.ws = self.peer.tensor(lay["ws"], (self.w.total,), torch.uint8)
@@ -424,8 +449,8 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         z_h, pm_h, ps, pe = make_config_inputs(args.config)
         N = z_h.shape[1]
         prec = args.precision or {0: "fp32", 1: "fp16"}.get(args.config, "bf16")
-        exchange = getattr(args, "exchange", "peer")
-        sp = ShardedPair(N, prec, dev, exchange=exchange)
+        sp = ShardedPair(N, prec, dev, exchange=getattr(args, "exchange", "peer"))
+        exchange = sp.exchange  # "nccl" if the peer mappings were refused on some rank
         packs = []
         for starting, p in ((True, ps), (False, pe)):
             m = TriangleAttention(starting=starting, precision=prec).to(dev)

@@ -10,8 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from boltz_mlx_b200.distributed import (blocks_to_cols, cols_to_blocks, cols_to_rows, from_blocks, gather_bias,
-                                        rows_to_cols, shard_rows, to_blocks)
+from boltz_mlx_b200.distributed import (all_ranks_ok, blocks_to_cols, cols_to_blocks, cols_to_rows, from_blocks,
+                                        gather_bias, rows_to_cols, shard_rows, to_blocks)
 from boltz_mlx_b200.layout import Workspace
 
 
@@ -98,3 +98,36 @@ def test_shard_rows_requires_divisibility():
     assert shard_rows(1024, 8, 3) == (384, 512)
     with pytest.raises(NotImplementedError):
         shard_rows(1000, 3, 0)
+
+
+def _agree_worker(rank, P, port, bad, errq):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=P)
+        # every rank learns whether all ranks succeeded (the peer exchange's set-up vote)
+        assert all_ranks_ok(True) is True
+        assert all_ranks_ok(rank != bad) is (bad < 0)
+        assert all_ranks_ok(False) is False
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+@pytest.mark.parametrize("P,bad", [(2, -1), (2, 1), (4, 2)])
+def test_all_ranks_ok_is_a_collective_vote(P, bad):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, P, port, bad, errq)) for r in range(P)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
