@@ -5,7 +5,7 @@ descriptors of the consumers read, for every MMA the kernels issue."""
 import numpy as np
 import pytest
 
-from boltz_mlx_b200.layout import TILE, Workspace, img_offsets, sw128_offsets
+from boltz_mlx_b200.layout import TILE, Workspace, bias16_offsets, img_offsets, sw128_offsets
 
 
 def kmajor_desc_addr(start, lbo, sbo, rows, kdim):
@@ -109,3 +109,28 @@ def test_workspace_regions_disjoint_and_aligned(N):
         for R in (1, max(1, N // 3), N):
             assert Workspace.make(2, N, R, dtype).off_bias == 0
             assert Workspace.make(2, N, R, dtype).off_q == w.off_q
+
+
+def test_square_image_mma_k_steps():
+    """The 128 x 128 MMAs (attention output projection, tri-mult tail: A = gated core / norm_out(o),
+    B = W_o / p_out): K steps of 16 at +256 B with lbo 128 / sbo 2048 cover the whole K-major image."""
+    off = img_offsets(TILE, 128)
+    for ks in range(8):
+        got = kmajor_desc_addr(ks * 256, 128, 16 * 128, TILE, 16)
+        assert np.array_equal(got, off[:, ks * 16:(ks + 1) * 16])
+
+
+@pytest.mark.parametrize("half", [0, 1])
+def test_tri_bias_block_reads_as_a_kmajor_operand(half):
+    """One 32 KB tri-bias block ([k/8][q][8] fp16, queries x keys) is a K-major operand with K core
+    matrices 2048 B apart (lbo) and 8-query groups 128 B apart (sbo): K steps of 16 keys start every
+    4096 B, so the keys 64 half .. 64 half + 63 of S are four steps from (8 half) x 2048."""
+    N = 256
+    NT = N // TILE
+    full = bias16_offsets(N, 1, NT)[0, 0]  # [q, k] byte offsets, batch 0 head 0
+    blk = full[:TILE, :TILE] - full[0, 0]  # block (qt 0, kt 0): offsets inside its 32 KB
+    assert blk.min() == 0 and blk.max() == 32768 - 2
+    for k4 in range(4):
+        k0 = 64 * half + 16 * k4
+        got = kmajor_desc_addr((8 * half + 2 * k4) * 2048, 2048, 128, TILE, 16)
+        assert np.array_equal(got, blk[:, k0:k0 + 16])
