@@ -131,3 +131,43 @@ def test_all_ranks_ok_is_a_collective_vote(P, bad):
         errs.append(errq.get())
     assert not errs, errs
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def _validation_worker(port, errq):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=0, world_size=1)
+        from boltz_mlx_b200 import _lib
+        from boltz_mlx_b200.distributed import ShardedPair
+
+        try:
+            ShardedPair(256, "bf16", torch.device("cpu"), exchange="allreduce")
+            raise AssertionError("unknown exchange accepted")
+        except ValueError:
+            pass
+        try:  # 16-bit tri-bias rows move in 128-row blocks: rows per rank must be a multiple of 128
+            ShardedPair(200, "bf16", torch.device("cpu"))
+            raise AssertionError("ragged 16-bit shard accepted")
+        except _lib.TriAttnUnsupported:
+            pass
+        sp = ShardedPair(200, "fp32", torch.device("cpu"))  # fp32 shards take any row count
+        assert (sp.r0, sp.r1, sp.exchange) == (0, 200, "nccl")
+        sp.close()  # no peer buffers: a no-op
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(repr(e))
+        raise
+
+
+def test_sharded_pair_validates_its_arguments():
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    p = ctx.Process(target=_validation_worker, args=(_free_port(), errq))
+    p.start()
+    p.join(timeout=120)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert p.exitcode == 0
