@@ -24,8 +24,40 @@ from typing import Optional
 import torch
 from torch import nn
 
+import contextlib
+import warnings
+
 from . import _lib
 from .layout import workspace_bytes
+
+
+@contextlib.contextmanager
+def nvtx_range(name: str):
+    """An NVTX range around one layer call (visible in Nsight timelines); a no-op where NVTX is absent."""
+    pushed = False
+    try:
+        torch.cuda.nvtx.range_push(name)
+        pushed = True
+    except Exception:  # noqa: BLE001 - tracing must never break a call
+        pass
+    try:
+        yield
+    finally:
+        if pushed:
+            try:
+                torch.cuda.nvtx.range_pop()
+            except Exception:  # noqa: BLE001
+                pass
+
+
+def run_with_fp32_fallback(run16, run32, all_finite) -> tuple:
+    """The reference's overflow guard (model.py:179-193: a 16-bit overflow triggers a recompute in
+    fp32), as control flow: run the 16-bit layer; if its output is not all finite, run the fp32 layer.
+    Returns (output, fell_back)."""
+    out = run16()
+    if all_finite(out):
+        return out, False
+    return run32(), True
 
 
 class Attention(nn.Module):
@@ -110,6 +142,10 @@ class TriangleAttention(nn.Module):
     # bias of all rows, then chunks of rows; attention.py:55-68).  At B = 1, 16-bit: N = 2048 needs
     # 5.4 GB and runs whole; N = 4096 needs 21 GB and runs in chunks.
     max_workspace_bytes: int = 8 << 30
+    # 16-bit precisions: check each output for inf / nan (one reduction and a host sync per call) and
+    # recompute the layer in fp32 when any is found, as the reference does on an fp16 overflow
+    fp32_fallback: bool = False
+    nonfinite_events: int = 0
 
     def chunk_rows(self, B: int, N: int, dtype: int, chunk_size: Optional[int] = None) -> int:
         """Rows per chunk for a B x N layer: `chunk_size` rounded up to a whole 128-row tile on the
@@ -145,21 +181,37 @@ class TriangleAttention(nn.Module):
             m = mask.to(device=z.device, dtype=torch.float32).contiguous()
         if out is None:
             out = torch.empty_like(z)
-        packed = self.packed_weights(dtype)
-        rows = self.chunk_rows(B, N, dtype, chunk_size)
-        nbytes = _lib.workspace_bytes(B, N, rows, dtype)
-        ws = self._ws.get(nbytes, z.device)
-        if rows == N:
-            _lib.check(_lib.lib().triattn_forward(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N,
-                                                  int(self.starting), float(self.inf), dtype, int(add_residual),
-                                                  out.data_ptr(), ws.data_ptr(), ws.numel(),
-                                                  _lib.stream_handle(z.device)))
-        else:
-            _lib.check(_lib.lib().triattn_forward_chunked(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N,
-                                                          int(self.starting), float(self.inf), dtype,
-                                                          int(add_residual), out.data_ptr(), rows, ws.data_ptr(),
-                                                          ws.numel(), _lib.stream_handle(z.device)))
-        return out
+
+        def launch(dt: int, dst: torch.Tensor) -> torch.Tensor:
+            packed = self.packed_weights(dt)
+            rows = self.chunk_rows(B, N, dt, chunk_size)
+            ws = self._ws.get(_lib.workspace_bytes(B, N, rows, dt), z.device)
+            if rows == N:
+                _lib.check(_lib.lib().triattn_forward(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N,
+                                                      int(self.starting), float(self.inf), dt, int(add_residual),
+                                                      dst.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                      _lib.stream_handle(z.device)))
+            else:
+                _lib.check(_lib.lib().triattn_forward_chunked(z.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N,
+                                                              int(self.starting), float(self.inf), dt,
+                                                              int(add_residual), dst.data_ptr(), rows,
+                                                              ws.data_ptr(), ws.numel(), _lib.stream_handle(z.device)))
+            return dst
+
+        with nvtx_range(f"triattn.{'start' if self.starting else 'end'}"):
+            if not self.fp32_fallback or dtype == _lib.F32:
+                return launch(dtype, out)
+            # guarded: never overwrite z in place before the 16-bit result is known to be finite
+            dst = torch.empty_like(z) if out.data_ptr() == z.data_ptr() else out
+            res, fell_back = run_with_fp32_fallback(lambda: launch(dtype, dst), lambda: launch(_lib.F32, dst),
+                                                    lambda t: bool(torch.isfinite(t).all()))
+            if fell_back:
+                self.nonfinite_events += 1
+                warnings.warn(f"TriangleAttention: non-finite {self.precision} output at N={N}; recomputed in fp32",
+                              RuntimeWarning, stacklevel=3)
+            if dst is not out:
+                out.copy_(res)
+            return out
 
     def forward(self, x: torch.Tensor, mask: Optional[torch.Tensor] = None, chunk_size: Optional[int] = None,
                 use_kernels: bool = False, xn: Optional[torch.Tensor] = None, keep_t: bool = False) -> torch.Tensor:
