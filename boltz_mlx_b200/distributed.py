@@ -119,6 +119,21 @@ def all_ranks_ok(ok: bool, group=None, device: Optional[torch.device] = None) ->
     return bool(int(t.item()))
 
 
+def exchange_intact(sent_blk: torch.Tensor, recv_blk: torch.Tensor, group=None) -> bool:
+    """Integrity check of a block all-to-all (blocks_to_cols / cols_to_blocks): block q of `sent_blk`
+    went to rank q, block p of `recv_blk` came from rank p.  Every rank sends the float64 sum of each
+    block it sent to the block's receiver, which compares it with the sum of what arrived.  True on
+    every rank iff every block arrived intact on every rank (one small all-to-all + one vote)."""
+    P = sent_blk.shape[0]
+    sent = sent_blk.reshape(P, -1).double().sum(1)
+    got = torch.empty_like(sent)
+    dist.all_to_all_single(got, sent.contiguous(), group=group)
+    arrived = recv_blk.reshape(P, -1).double().sum(1)
+    tol = 1e-9 * (arrived.abs() + 1.0)
+    ok = bool(((got - arrived).abs() <= tol).all())
+    return all_ranks_ok(ok, group, sent_blk.device)
+
+
 class PeerUnavailable(RuntimeError):
     """Some rank could not map another rank's buffer (no peer access between those GPUs)."""
 

@@ -10,8 +10,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from boltz_mlx_b200.distributed import (all_ranks_ok, blocks_to_cols, cols_to_blocks, cols_to_rows, from_blocks,
-                                        gather_bias, rows_to_cols, shard_rows, to_blocks)
+from boltz_mlx_b200.distributed import (all_ranks_ok, blocks_to_cols, cols_to_blocks, cols_to_rows,
+                                        exchange_intact, from_blocks, gather_bias, rows_to_cols, shard_rows,
+                                        to_blocks)
 from boltz_mlx_b200.layout import Workspace
 
 
@@ -171,3 +172,57 @@ def test_sharded_pair_validates_its_arguments():
         errs.append(errq.get())
     assert not errs, errs
     assert p.exitcode == 0
+
+
+def _fault_worker(rank, P, port, mode, errq):
+    """mode 'corrupt': rank 1 damages one received block; every rank must see the exchange fail.
+    mode 'absent': rank 1 leaves before the exchange; the others must get an error within the
+    process-group timeout (no hang)."""
+    from datetime import timedelta
+
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=P, timeout=timedelta(seconds=5))
+        R, C = 4, 8
+        z_blk = torch.randn(P, R, R, C, generator=torch.Generator().manual_seed(rank))
+        if mode == "absent" and rank == 1:
+            return  # leaves without joining the exchange (the host-side stand-in for a dead rank)
+        recv = torch.empty_like(z_blk)
+        try:
+            blocks_to_cols(z_blk, recv)
+        except RuntimeError:
+            assert mode == "absent", "the exchange failed without a fault"
+            errq.put(f"ok rank {rank}: detected")
+            return
+        assert mode != "absent", "the exchange completed without the absent rank"
+        assert exchange_intact(z_blk, recv), "intact exchange reported as damaged"
+        if rank == 1:
+            recv[0, 0, 0, 0] += 1.0  # a corrupted shard
+        assert exchange_intact(z_blk, recv) is False, "damaged block not detected"
+        errq.put(f"ok rank {rank}: detected")
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+@pytest.mark.parametrize("mode", ["corrupt", "absent"])
+def test_exchange_faults_are_detected_on_the_host(mode):
+    P = 3
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_worker, args=(r, P, port, mode, errq)) for r in range(P)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    msgs = []
+    while not errq.empty():
+        msgs.append(errq.get())
+    bad = [m for m in msgs if not m.startswith("ok")]
+    assert not bad, bad
+    expect = P if mode == "corrupt" else P - 1
+    assert sum(m.startswith("ok") for m in msgs) == expect, msgs
