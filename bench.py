@@ -474,6 +474,7 @@ def run_b200(args):
 
     line = {
         "metric": metric_name(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": 1,
+        "gpu": torch.cuda.get_device_name(dev), "host_cores": os.cpu_count(),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "ms_per_layer": step_ms / layers,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": prec,
         "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
@@ -555,7 +556,8 @@ def run_trimul(args):
     fl = trimul_flops(N)
     line = {
         "metric": f"tri-mult TFLOP/s, outgoing+incoming pair, N={N}, B=1", "layer": "trimul",
-        "value": 2 * fl["total"] / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "value": 2 * fl["total"] / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
+        "gpu": torch.cuda.get_device_name(dev), "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "ms_per_layer": step_ms / 2, "higher_is_better": True,
         "dtype": prec, "data": "synthetic: the config's pair tensor and mask, seeded N(0,1/128) weights",
         "config": {"workload": f"config{args.config}: tri-mult outgoing + incoming, N={N}, c_z=128, {prec}",

@@ -568,6 +568,7 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         if rank == 0:
             line = {
                 "metric": metric_name(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": ws_n,
+                "gpu": torch.cuda.get_device_name(dev), "host_cores": os.cpu_count(),
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "ms_per_layer": step_ms / 2,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": prec,
                 "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
