@@ -45,7 +45,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .layout import C_IN, HEADS, Workspace
+from .layout import C_IN, Workspace
 
 
 def shard_rows(N: int, P: int, rank: int) -> tuple[int, int]:

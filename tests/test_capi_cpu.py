@@ -1,7 +1,6 @@
 """CPU: libtriattn.so loads, exports every symbol include/triattn.h declares, and its host-side logic
 (argument validation, workspace layout) behaves -- no kernel is launched here."""
 
-import ctypes
 import re
 from pathlib import Path
 

@@ -7,9 +7,9 @@ import pytest
 import torch
 
 from boltz_mlx_b200 import _lib
-from oracle.triattn_ref import make_inputs, make_params, metrics, tri_attention_ref
+from oracle.triattn_ref import make_inputs, make_params, tri_attention_ref
 from tests._util import assert_parity, module, rand_mask
-from tests.test_oracle import GOLDEN, golden_case, golden_cases
+from tests.test_oracle import golden_case, golden_cases
 
 pytestmark = pytest.mark.gpu
 PRECISIONS = ["fp32", "bf16", "fp16"]

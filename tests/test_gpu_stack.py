@@ -4,7 +4,6 @@ oracle at max_rel <= 1e-5 per layer.  The 16-bit error of every layer stays boun
 compounding: the final z and the accumulated update both track the fp32 stack."""
 
 import pytest
-import torch
 
 import bench
 
