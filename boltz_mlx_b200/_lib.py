@@ -138,7 +138,7 @@ def stream_handle(device: torch.device) -> int:
 
 
 def device_status(clear: bool = True) -> int:
-    """The device status word (0 = ok; 101..103 = a bounded wait ran out, 104 bad index, 105 unaligned
+    """The device status word (0 = ok; 101..103 = a bounded wait ran out, 105 unaligned
     shared memory, 106 a cross-GPU barrier missed a peer).  Synchronises."""
     v = ctypes.c_int(0)
     check(lib().triattn_device_status(ctypes.byref(v), int(clear)))

@@ -5,7 +5,11 @@
 // whose memory is carved up once by an allocator it does not own, or code that must keep a fixed
 // device footprint known at load time.  For them the layer's scratch (the tri-bias table, the
 // q/k/v/g operand images, the attention output before projection and the mask bias) lives in the
-// fixed array below, which every GPU that loads libtriattn.so holds from load until process exit.
+// fixed array below.  A GPU holds the array from the moment this file's module is loaded on it until
+// process exit: under CUDA's default lazy module loading (CUDA_MODULE_LOADING=LAZY) that is the first
+// triattn_forward_noalloc call on the device, whose symbol lookup loads the module and reserves the
+// 48 MiB; with CUDA_MODULE_LOADING=EAGER it is library load.  A caller that hands the rest of its
+// device memory to another allocator should make one small call (e.g. N = 1) on each device first.
 //
 // Limits and rules:
 //   * The array holds kScratchBytes = 48 MiB.  A call is accepted when its workspace,
@@ -45,6 +49,10 @@ int scratch_for_current_device(void** out) {
   if (!cache[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e == cudaErrorMemoryAllocation)
+      return triattn::record_error(TRIATTN_ECUDA, "cudaGetSymbolAddress(scratch)",
+                                   "no device memory left for the 48 MiB scratch array (reserved when the "
+                                   "module loads, on the first call under lazy loading)");
     if (e != cudaSuccess || p == nullptr)
       return triattn::record_error(TRIATTN_ECUDA, "cudaGetSymbolAddress(scratch)", cudaGetErrorString(e));
     cache[dev] = p;

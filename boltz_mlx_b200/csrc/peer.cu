@@ -4,8 +4,11 @@
 // epoch e: lane t (< world) publishes e into slot [rank] of rank t's block (a system-scope release
 // store over NVLink), then waits until slot [t] of its own block holds e or later (system-scope
 // acquire loads).  Epochs only grow, so a late signal from the previous barrier cannot satisfy this
-// one.  The wait is bounded: after TRIATTN_WAIT_NS (or as soon as the status word holds an error)
-// the lane records DEV_PEER_TIMEOUT and returns, so a rank that never arrives cannot hang this GPU.
+// one.  The wait is bounded: after TRIATTN_WAIT_NS (or as soon as a kernel records an error while
+// this barrier waits) the lane records DEV_PEER_TIMEOUT and returns, so a rank that never arrives
+// cannot hang this GPU.  An error already in the status word when the barrier starts (a stale one,
+// from an earlier launch) does not end the wait: skipping a barrier would let the exchange's remote
+// stores race, so every barrier waits for every peer unless a NEW error appears meanwhile.
 #include <algorithm>
 #include <cstdint>
 
@@ -28,6 +31,7 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const unsigned long lo
                                                           int world, unsigned epoch, int* status) {
   const int t = threadIdx.x;
   if (t >= world) return;
+  const int status_at_entry = *reinterpret_cast<volatile int*>(status);
   __threadfence_system();  // this GPU's earlier writes (previous kernels included) before the signal
   st_release_sys(reinterpret_cast<unsigned*>(flag_ptrs[t]) + rank, epoch);
   const unsigned* mine = reinterpret_cast<const unsigned*>(flag_ptrs[rank]) + t;
@@ -35,7 +39,7 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const unsigned long lo
   for (uint32_t spin = 0;; ++spin) {
     if (static_cast<int>(ld_acquire_sys(mine) - epoch) >= 0) break;
     if ((spin & 63u) == 0u) {
-      if (*reinterpret_cast<volatile int*>(status) != 0) return;
+      if (*reinterpret_cast<volatile int*>(status) != status_at_entry) return;  // a new error meanwhile
       const uint64_t now = global_timer_ns();
       if (t0 == 0) {
         t0 = now;

@@ -22,7 +22,6 @@ enum DeviceError : int {
   DEV_TIMEOUT_TMA = 101,
   DEV_TIMEOUT_MMA = 102,
   DEV_TIMEOUT_SYNC = 103,
-  DEV_BAD_INDEX = 104,
   DEV_BAD_ALIGN = 105,  // shared-memory base not aligned as a swizzled operand needs
   DEV_PEER_TIMEOUT = 106,  // a cross-GPU barrier did not see every peer's signal in time
 };

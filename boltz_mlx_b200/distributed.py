@@ -123,14 +123,21 @@ def exchange_intact(sent_blk: torch.Tensor, recv_blk: torch.Tensor, group=None) 
     """Integrity check of a block all-to-all (blocks_to_cols / cols_to_blocks): block q of `sent_blk`
     went to rank q, block p of `recv_blk` came from rank p.  Every rank sends the float64 sum of each
     block it sent to the block's receiver, which compares it with the sum of what arrived.  True on
-    every rank iff every block arrived intact on every rank (one small all-to-all + one vote)."""
+    every rank iff every block arrived intact on every rank (one small all-to-all + one vote).
+
+    A diagnostic of the NCCL exchange, not run on the hot path (it costs a pass over the blocks and a
+    host sync): call it after an exchange when verifying a deployment.  A block whose sum is inf or NaN
+    on both sides (non-finite data sent intact) counts as intact."""
     P = sent_blk.shape[0]
     sent = sent_blk.reshape(P, -1).double().sum(1)
     got = torch.empty_like(sent)
     dist.all_to_all_single(got, sent.contiguous(), group=group)
     arrived = recv_blk.reshape(P, -1).double().sum(1)
-    tol = 1e-9 * (arrived.abs() + 1.0)
-    ok = bool(((got - arrived).abs() <= tol).all())
+    tol = 1e-9 * (arrived.abs().nan_to_num(posinf=0.0) + 1.0)
+    close = (got - arrived).abs() <= tol
+    same_nonfinite = (~torch.isfinite(got)) & (~torch.isfinite(arrived)) & (
+        (got.isnan() & arrived.isnan()) | (got == arrived))
+    ok = bool((close | same_nonfinite).all())
     return all_ranks_ok(ok, group, sent_blk.device)
 
 
@@ -249,10 +256,15 @@ class ShardedPair:
     """One start+end triangle-attention pair on a row-sharded pair tensor (B = 1)."""
 
     def __init__(self, N: int, precision: str, device: torch.device, group=None, inf: float = 1e9,
-                 exchange: str = "nccl"):
+                 exchange: str = "nccl", checked: bool = True):
         if exchange not in ("nccl", "peer"):
             raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
         self.N, self.inf, self.device, self.group, self.exchange = N, inf, device, group, exchange
+        # checked: read the device status word after every pair (one host sync) and raise on any
+        # error, so a bounded wait that ran out (a peer that never arrived, a stale error) is reported
+        # instead of returning blocks whose exchange may have raced.  Timing loops may turn it off and
+        # read the status once at the end.
+        self.checked = checked
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.r0, self.r1 = shard_rows(N, self.P, self.rank)
@@ -416,20 +428,40 @@ class ShardedPair:
                                          dt, 1, ws, nb, st))
         self.barrier()
 
+    def check_status(self, when: str) -> None:
+        """Raise TriAttnError on EVERY rank when the device status word of ANY rank holds an error (one
+        small all-reduce MAX, so no rank goes on into the next exchange while another has stopped).  The
+        word is cleared on read, so the next pair starts clean."""
+        own = _lib.device_status(clear=True)
+        v = torch.tensor([own], dtype=torch.int32, device=self.device)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.group)
+        worst = int(v.item())
+        if worst != 0:
+            raise _lib.TriAttnError(_lib.EDEVICE, f"device status {worst} {when} (this rank {self.rank} of {self.P}: "
+                                                  f"{own}; 106 = a cross-GPU barrier ran out of time)")
+
     def pair_blocks(self, z_blk, mask, packed_start, packed_end) -> None:
         """One start+end pair on the block-layout residual stream.  nccl: two all-to-alls, no copies.
-        peer: z_blk should be self.zb (the shared buffer; anything else is copied in and out)."""
+        peer: z_blk should be self.zb (the shared buffer; anything else is copied in and out).
+        checked mode: an error recorded before the pair raises before any launch; one recorded during
+        the pair raises after it (the blocks are then not to be used)."""
+        if self.checked:
+            self.check_status("before the pair")
         if self.exchange == "peer":
             own = z_blk.data_ptr() == self.zb.data_ptr()
             if not own:
                 self.zb.copy_(z_blk)
             self.start_peer(mask, packed_start)
             self.end_peer(mask, packed_end)
+            if self.checked:
+                self.check_status("after the pair")
             if not own:
                 z_blk.copy_(self.zb)
             return
         self.start_blocks(z_blk, mask, packed_start)
         self.end_blocks(z_blk, mask, packed_end)
+        if self.checked:
+            self.check_status("after the pair")
 
     def pair(self, z_loc, mask, packed_start, packed_end) -> None:
         """One start+end pair on a row-layout shard z_loc [R, N, 128] (converted to blocks and back)."""
@@ -464,7 +496,8 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         z_h, pm_h, ps, pe = make_config_inputs(args.config)
         N = z_h.shape[1]
         prec = args.precision or {0: "fp32", 1: "fp16"}.get(args.config, "bf16")
-        sp = ShardedPair(N, prec, dev, exchange=getattr(args, "exchange", "peer"))
+        # unchecked in the timed loop (no host sync per step); the status is read on every rank at the end
+        sp = ShardedPair(N, prec, dev, exchange=getattr(args, "exchange", "peer"), checked=False)
         exchange = sp.exchange  # "nccl" if the peer mappings were refused on some rank
         packs = []
         for starting, p in ((True, ps), (False, pe)):

@@ -72,7 +72,7 @@ TRIATTN_API const char* triattn_version(void);
 TRIATTN_API const char* triattn_last_error_string(void);
 
 /* Read the device status word of the current device (0 = ok; 101 a bulk copy, 102 an MMA, 103 a
- * barrier wait ran out; 104 an index check failed; 105 a shared-memory base was not aligned as a
+ * barrier wait ran out; 105 a shared-memory base was not aligned as a
  * swizzled operand needs; 106 a cross-GPU barrier missed a peer); clear it when `clear` != 0.
  * Synchronises the device.  Returns TRIATTN_OK and writes the word to *status. */
 TRIATTN_API int triattn_device_status(int* status, int clear);
@@ -264,7 +264,9 @@ TRIATTN_API int triattn_trimul_forward_addln(const float* z, const float* mask, 
  * No counterpart in the reference.  triattn_forward without a workspace argument, for callers that
  * cannot allocate device memory at run time (a plugin host that forbids cudaMalloc after start-up,
  * a process whose device memory is owned by another allocator, a fixed device footprint).  The
- * scratch is a 48 MiB array inside the library that every GPU loading it holds until exit; calls
+ * scratch is a 48 MiB array inside the library; a GPU holds it from the first call on that device
+ * (CUDA's default lazy module loading reserves it then; eager loading at library load) until exit,
+ * so make one small call per device at start-up, before handing memory to another allocator.  Calls
  * whose triattn_workspace_bytes(B, N, N, dtype) exceeds it (about N > 128 at B = 1) return
  * TRIATTN_ENOSPACE.  The first call on a device looks the array up (make it before any stream
  * capture); calls share the array, so calls that overlap on the GPU race.  Allocates nothing. */

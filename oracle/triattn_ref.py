@@ -85,14 +85,28 @@ def _layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tens
 
 def tri_attention_ref(z: torch.Tensor, mask: Optional[torch.Tensor], params: dict, *, starting: bool = True,
                       inf: float = DEFAULT_INF, dtype: torch.dtype = torch.float32,
-                      chunk_rows: Optional[int] = None, rows: Optional[tuple] = None) -> torch.Tensor:
+                      chunk_rows: Optional[int] = None, rows: Optional[tuple] = None,
+                      row_ids: Optional[list] = None) -> torch.Tensor:
     """y = TriangleAttention(z, mask) on the CPU in `dtype` (float32 = the reference's fp32 path,
     float64 = the error-budget reference).  z: [B, N, N, 128]; mask: [B, N, N] or None.
     Returns the update y [B, N, N, 128] in z's orientation.
 
     rows=(r0, r1): compute only attention rows r0..r1-1 (rows are independent once the tri bias of
     all rows is known, attention.py:55-68) and return them in ATTENTION orientation,
-    [B, r1-r0, N, 128] (for the ending node attention row a is column a of z)."""
+    [B, r1-r0, N, 128] (for the ending node attention row a is column a of z).
+    row_ids=[a0, a1, ...]: the same for an arbitrary list of attention rows (the LayerNorm and the tri
+    bias are computed once), [B, len(row_ids), N, 128] in the listed order."""
+    if row_ids is not None:
+        x = z.to(dtype)
+        m = torch.ones(x.shape[:-1], dtype=dtype) if mask is None else mask.to(dtype)
+        if not starting:
+            x = x.transpose(-2, -3)
+            m = m.transpose(-1, -2)
+        P = {k: (v.to(dtype) if v is not None else None) for k, v in params.items()}
+        xn = _layer_norm(x, P["ln_w"], P["ln_b"])
+        tri_bias = (xn @ P["w_b"].T).permute(0, 3, 1, 2)  # [B, H, Q, K] from ALL rows
+        out = [_rows_attention(xn[:, a:a + 1], m[:, a:a + 1], tri_bias, P, inf, dtype) for a in row_ids]
+        return torch.cat(out, 1)
     x = z.to(dtype)
     if mask is None:
         mask = torch.ones(x.shape[:-1], dtype=dtype)
@@ -138,6 +152,30 @@ def tri_attention_ref(z: torch.Tensor, mask: Optional[torch.Tensor], params: dic
     if not starting:
         y = y.transpose(-2, -3)
     return y
+
+
+def _rows_attention(xc: torch.Tensor, mc: torch.Tensor, tri_bias: torch.Tensor, P: dict, inf: float,
+                    dtype: torch.dtype) -> torch.Tensor:
+    """Attention rows of LayerNorm output xc [B, Ic, J, 128] with mask rows mc [B, Ic, K] and the tri bias
+    of all rows [B, H, Q, K] (attention.py:80-89, the same steps as the chunk loop above)."""
+    B, Ic, J = xc.shape[:3]
+    wq = torch.cat([P["w_q"], P["w_k"], P["w_v"], P["w_g"]], 0)
+    h = xc @ wq.T
+    q = h[..., :HC].reshape(B * Ic, J, HEADS, C_HEAD).permute(0, 2, 1, 3)
+    k = h[..., HC:2 * HC].reshape(B * Ic, J, HEADS, C_HEAD).permute(0, 2, 1, 3)
+    v = h[..., 2 * HC:3 * HC].reshape(B * Ic, J, HEADS, C_HEAD).permute(0, 2, 1, 3)
+    g = h[..., 3 * HC:4 * HC]
+    if P.get("g_b") is not None:
+        g = g + P["g_b"]
+    mask_bias = (inf * (mc - 1))[:, :, None, None, :]
+    bias = (tri_bias[:, None] + mask_bias).reshape(B * Ic, HEADS, J, J)
+    a = (q * C_HEAD ** -0.5) @ k.transpose(-1, -2) + bias
+    if dtype != torch.float32:
+        masked = (mask_bias != 0).expand(B, Ic, HEADS, J, J).reshape(a.shape)
+        a = torch.where(masked, a.float().to(dtype), a)
+    a = torch.softmax(a, dim=-1)
+    o = (a @ v).permute(0, 2, 1, 3).reshape(B, Ic, J, HC)
+    return (o * torch.sigmoid(g)) @ P["w_o"].T
 
 
 def tri_attention_np64(z: np.ndarray, mask: Optional[np.ndarray], params: dict, *, starting: bool = True,

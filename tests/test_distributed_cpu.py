@@ -197,6 +197,13 @@ def _fault_worker(rank, P, port, mode, errq):
             return
         assert mode != "absent", "the exchange completed without the absent rank"
         assert exchange_intact(z_blk, recv), "intact exchange reported as damaged"
+        # non-finite data sent intact is intact: every rank sends NaN / inf in one block
+        z_nf = z_blk.clone()
+        z_nf[0, 0, 0, 0] = float("nan")
+        z_nf[-1, 0, 0, 1] = float("inf")
+        recv_nf = torch.empty_like(z_nf)
+        blocks_to_cols(z_nf, recv_nf)
+        assert exchange_intact(z_nf, recv_nf), "non-finite but intact blocks reported as damaged"
         if rank == 1:
             recv[0, 0, 0, 0] += 1.0  # a corrupted shard
         assert exchange_intact(z_blk, recv) is False, "damaged block not detected"
@@ -226,3 +233,64 @@ def test_exchange_faults_are_detected_on_the_host(mode):
     assert not bad, bad
     expect = P if mode == "corrupt" else P - 1
     assert sum(m.startswith("ok") for m in msgs) == expect, msgs
+
+
+def _checked_pair_worker(rank, world, port, errq):
+    """ShardedPair in checked mode on gloo ranks, with the library's status read faked on the host:
+    a stale error on one rank makes EVERY rank raise before launching anything, and an error recorded
+    during a pair makes every rank raise after it instead of returning the blocks."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from boltz_mlx_b200 import _lib
+        from boltz_mlx_b200 import distributed as tdist
+
+        sp = tdist.ShardedPair(256, "bf16", torch.device("cpu"))
+        assert sp.checked
+        launched = []
+        sp.start_blocks = lambda *a: launched.append("start")
+        sp.end_blocks = lambda *a: launched.append("end")
+        z_blk = torch.zeros(world, sp.R, sp.R, 4)
+        # 1) stale error on rank 1 only (e.g. an earlier barrier timed out there)
+        reads = iter([106 if rank == 1 else 0])
+        _lib.device_status = lambda clear=True: next(reads, 0)
+        try:
+            sp.pair_blocks(z_blk, None, None, None)
+            raise AssertionError("stale status not reported")
+        except _lib.TriAttnError as e:
+            assert "106" in str(e), str(e)
+        assert launched == [], launched
+        # 2) clean before, an error recorded during the pair on rank 0
+        reads = iter([0, 102 if rank == 0 else 0])
+        _lib.device_status = lambda clear=True: next(reads, 0)
+        try:
+            sp.pair_blocks(z_blk, None, None, None)
+            raise AssertionError("in-pair error not reported")
+        except _lib.TriAttnError as e:
+            assert "102" in str(e), str(e)
+        assert launched == ["start", "end"], launched
+        # 3) clean: the pair returns
+        _lib.device_status = lambda clear=True: 0
+        sp.pair_blocks(z_blk, None, None, None)
+        assert launched == ["start", "end", "start", "end"]
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+def test_checked_pair_reports_device_errors_on_every_rank():
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_checked_pair_worker, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from boltz_mlx_b200 import _lib
-from oracle.triattn_ref import make_inputs, make_params, tri_attention_ref
+from oracle.triattn_ref import make_params, tri_attention_ref
 from tests._util import assert_parity, module, rand_mask
 from tests.test_oracle import golden_case, golden_cases
 
@@ -122,21 +122,3 @@ def test_row_chunked_stages_equal_full(precision):
                                           out.data_ptr(), ws.data_ptr(), ws.numel(), st))
         torch.cuda.synchronize()
         assert torch.equal(out, full)
-
-
-@pytest.mark.parametrize("cfg", [1, 2, 4])
-def test_benchmark_configs_sampled_rows(cfg):
-    """Configs 1 (N=384 fp16), 2 (N=1024 bf16) and 4 (N=2048 bf16) at full size: start + end pair vs
-    the oracle on a sample of attention rows (first, last, padded and interior rows)."""
-    z, pm, p = make_inputs(cfg)
-    precision = {1: "fp16", 2: "bf16", 4: "bf16"}[cfg]
-    N = z.shape[1]
-    zc, mc = z.cuda(), pm.cuda()
-    n_pad = int((pm[0, 0] == 0).sum())
-    rows = sorted({0, 1, N // 2, N - n_pad - 1, N - 1} | ({N - n_pad} if n_pad else set()))
-    for starting in (True, False):
-        y = module(p, starting, precision)(zc, mc).cpu()
-        ya = y if starting else y.transpose(1, 2)
-        for r in rows:
-            ref = tri_attention_ref(z, pm, p, starting=starting, rows=(r, r + 1))
-            assert_parity(ya[:, r:r + 1], ref, precision, f"cfg{cfg} start={starting} row {r}")

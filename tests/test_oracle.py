@@ -91,6 +91,25 @@ def test_row_range_and_chunking_match_full():
         assert metrics(part.numpy(), ref.numpy())["max_rel"] <= 1e-6
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_row_ids_match_row_ranges(dtype):
+    """The row-list selection (one LayerNorm / tri-bias pass, any rows in any order) equals the row-range
+    path row by row, including a fully masked row."""
+    N = 19
+    g = torch.Generator().manual_seed(12)
+    z = torch.randn(1, N, N, 128, generator=g)
+    m = (torch.rand(1, N, N, generator=g) > 0.3).float()
+    m[:, 6, :] = 0
+    p = make_params(12, gate_bias=1.0, ln_identity=False)
+    ids = [18, 0, 6, 7, 3]
+    for starting in (True, False):
+        sel = tri_attention_ref(z, m, p, starting=starting, dtype=dtype, row_ids=ids)
+        assert sel.shape == (1, len(ids), N, 128)
+        for i, a in enumerate(ids):
+            one = tri_attention_ref(z, m, p, starting=starting, dtype=dtype, rows=(a, a + 1))
+            assert metrics(sel[:, i:i + 1].numpy(), one.numpy())["max_rel"] <= (1e-6 if dtype == torch.float32 else 1e-13)
+
+
 def test_ending_node_is_starting_node_on_transpose():
     N = 15
     g = torch.Generator().manual_seed(4)
