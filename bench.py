@@ -336,6 +336,61 @@ def workload_config(cfg_id, ws):
 
 
 # ---- B200 arm --------------------------------------------------------------------------------------
+def time_pair_one_gpu(cfg_id: int, dev, steps: int, warmup: int, precision=None) -> dict:
+    """One configuration's start+end pair on one GPU through triattn_forward, inputs resident in HBM:
+    ms per step (CUDA events over `steps` pairs after `warmup`) and the attention core alone."""
+    from boltz_mlx_b200 import _lib
+    from boltz_mlx_b200.triangle_attention import TriangleAttention, load_params
+
+    cfg = CONFIGS[cfg_id]
+    N = cfg["N"]
+    prec = precision or cfg["dtype"]
+    dt = _lib.dtype_code(prec)
+    z_h, pm_h, ps, pe = make_config_inputs(cfg_id)
+    packs = []
+    for starting, p in ((True, ps), (False, pe)):
+        m = TriangleAttention(starting=starting, precision=prec).to(dev)
+        load_params(m, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
+        packs.append(m.packed_weights(dt))
+    z, mask = z_h.to(dev), pm_h.to(dev)
+    t1, t2 = torch.empty_like(z), torch.empty_like(z)
+    wsb = _lib.workspace_bytes(1, N, N, dt)
+    work = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step():
+        _lib.check(L.triattn_forward(z.data_ptr(), mask.data_ptr(), packs[0].data_ptr(), 1, N, 1, 1e9, dt, 1,
+                                     t1.data_ptr(), work.data_ptr(), wsb, sh))
+        _lib.check(L.triattn_forward(t1.data_ptr(), mask.data_ptr(), packs[1].data_ptr(), 1, N, 0, 1e9, dt, 1,
+                                     t2.data_ptr(), work.data_ptr(), wsb, sh))
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    step_ms = e0.elapsed_time(e1) / steps
+    for _ in range(2):
+        _lib.check(L.triattn_core(1, N, 0, N, dt, work.data_ptr(), wsb, sh))
+    e0.record(stream)
+    for _ in range(5):
+        _lib.check(L.triattn_core(1, N, 0, N, dt, work.data_ptr(), wsb, sh))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "device status word set"
+    fl = layer_flops(N)
+    core_ms = e0.elapsed_time(e1) / 5
+    return {"metric": metric_name(cfg_id), "config": workload_config(cfg_id, 1), "precision": prec,
+            "ms_per_step": step_ms, "ms_per_layer": step_ms / 2, "tflops": 2 * fl["total"] / (step_ms * 1e-3) / 1e12,
+            "core_ms": core_ms, "core_tflops": fl["core"] / (core_ms * 1e-3) / 1e12, "steps": steps, "warmup": warmup}
+
+
 def run_b200(args):
     from boltz_mlx_b200 import _lib
     from boltz_mlx_b200.triangle_attention import TriangleAttention, load_params
@@ -476,6 +531,11 @@ def run_b200(args):
     assert torch.equal(ohs[0], ohs[1]), "pipelined e2e slots disagree"
     oh = ohs[0]
 
+    # ---- config 4 (N=2048), where the north star's scaling target is quoted: the same pair on this GPU ----
+    nested = None
+    if args.config == 2:
+        nested = time_pair_one_gpu(4, dev, args.steps, args.warmup, args.precision)
+
     # ---- CPU baseline (oracle on the host cores, bounded sample) ----
     threads = os.cpu_count() or 1
     cpu_pair_s, sample = cpu_pair_seconds(args.config, threads, budget_s=args.cpu_budget)
@@ -499,6 +559,8 @@ def run_b200(args):
         "gpu_launches": args.steps * layers * 4,
         "clocks": clk.summary(),
     }
+    if nested is not None:
+        line["config4_same_gpus"] = nested
     print(json.dumps(line), flush=True)
 
 

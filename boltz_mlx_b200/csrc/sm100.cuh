@@ -206,6 +206,20 @@ __device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[NR]) {
   for (int i = 0; i < NR; ++i) asm volatile("" : "+r"(r[i]));
 }
 
+// 8 consecutive 32-bit TMEM columns of this thread's lane -> 8 registers (warp-collective).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+// 8 registers -> 8 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // 32 registers -> 32 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(

@@ -39,6 +39,7 @@ from __future__ import annotations
 import ctypes
 import json
 import os
+from pathlib import Path
 from typing import Optional
 
 import torch
@@ -479,12 +480,98 @@ class ShardedPair:
         return 2 * bias + 2 * a2a
 
 
+def _time_sharded_pair(cfg_id, args, dev, make_config_inputs, layer_flops, peaks):
+    """Build a ShardedPair for configuration cfg_id, time args.steps pairs (max over ranks) and the attention
+    core alone; returns (record dict, sp, packs, mask, z_loc, z_h, pm_h, stream).  The caller closes sp."""
+    from .triangle_attention import TriangleAttention, load_params
+
+    z_h, pm_h, ps, pe = make_config_inputs(cfg_id)
+    N = z_h.shape[1]
+    prec = args.precision or {0: "fp32", 1: "fp16"}.get(cfg_id, "bf16")
+    # unchecked in the timed loop (no host sync per step); the status is read on every rank at the end
+    sp = ShardedPair(N, prec, dev, exchange=getattr(args, "exchange", "peer"), checked=False)
+    exchange = sp.exchange  # "nccl" if the peer mappings were refused on some rank
+    packs = []
+    for starting, p in ((True, ps), (False, pe)):
+        m = TriangleAttention(starting=starting, precision=prec).to(dev)
+        load_params(m, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
+        packs.append(m.packed_weights(sp.dt))
+    mask = pm_h[0].contiguous().to(dev)
+    z_loc = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
+    # the residual stream stays in block layout across steps (the layout the exchange uses)
+    z_blk = to_blocks(z_loc, sp.P, sp.zb if exchange == "peer" else torch.empty(sp.P, sp.R, sp.R, C_IN, device=dev))
+
+    def step():  # in place: every step is the same work on the updated shard
+        sp.pair_blocks(z_blk, mask, packs[0], packs[1])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    step_ms = float(ms)
+    fl = layer_flops(N)
+    pair_flops = 2 * fl["total"]
+
+    # dominant kernel: the attention core on this rank's rows (end-layer workspace), timed alone;
+    # max over ranks
+    st = _lib.stream_handle(dev)
+    L = _lib.lib()
+    for _ in range(2):
+        _lib.check(L.triattn_core(1, N, sp.r0, sp.r1, sp.dt, sp.ws.data_ptr(), sp.ws.numel(), st))
+    ev0.record(stream)
+    for _ in range(5):
+        _lib.check(L.triattn_core(1, N, sp.r0, sp.r1, sp.dt, sp.ws.data_ptr(), sp.ws.numel(), st))
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    core = torch.tensor([ev0.elapsed_time(ev1) / 5], device=dev)
+    dist.all_reduce(core, op=dist.ReduceOp.MAX)
+    core_ms = float(core)
+    pk, pk_kind = peaks()
+    tensor_peak = pk.get("bf16_tflops", 1590.0)
+    achieved = fl["core"] * sp.R / N / (core_ms * 1e-3) / 1e12
+    traffic = None
+    tf = Path(__file__).resolve().parents[1] / "profiles" / "core_traffic.json"
+    if tf.exists():
+        try:
+            full = json.loads(tf.read_text()).get(str(N))
+            # one core launch's DRAM bytes at this N (ncu, all N rows), scaled to this rank's R rows: the
+            # core reads each row's q, k, v images and writes its output once, so traffic grows with R
+            traffic = None if full is None else full * sp.R / N
+        except ValueError:
+            traffic = None
+    rec = {"N": N, "precision": prec, "ms_per_step": step_ms, "ms_per_layer": step_ms / 2,
+           "tflops": pair_flops / (step_ms * 1e-3) / 1e12, "rows_per_rank": sp.R,
+           "nvlink_bytes_per_rank_per_step": sp.nvlink_bytes_per_pair(),
+           "exchange": {"peer": "peer stores from the output projection + cross-GPU barrier (CUDA IPC)",
+                        "nccl": "NCCL all_to_all_single"}[exchange],
+           "roofline": {"bound": "tensor", "kernel": "core_tc (flash attention core, this rank's rows)",
+                        "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+                        "frac": achieved / tensor_peak, "peak_kind": f"{pk_kind} bf16 burst, per GPU",
+                        "traffic": traffic,
+                        "traffic_note": "ncu DRAM bytes of one full-N core launch (profiles/core_traffic.json) x R/N",
+                        "core_ms": core_ms,
+                        "algorithmic": f"F_core * R / N = {fl['core'] * sp.R / N:.4g} FLOP per launch"},
+           "gpu_launches": args.steps * 2 * (7 if exchange == "peer" else 4)}
+    return rec, sp, packs, mask, z_loc, z_h, pm_h, stream
+
+
 def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric_name, ClockSampler,
                   physical_gpu_index, peaks):
-    """bench.py --gpus P under torchrun: one start+end pair on the row-sharded pair tensor per step."""
+    """bench.py --gpus P under torchrun: one start+end pair on the row-sharded pair tensor per step; the
+    headline configuration, then (for config 2) config 4 (N=2048) at the same P as a nested record."""
     from datetime import timedelta
-
-    from .triangle_attention import TriangleAttention, load_params
 
     ws_n = int(os.environ["WORLD_SIZE"])
     rank = int(os.environ["RANK"])
@@ -492,66 +579,15 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    sp = None
     try:
-        z_h, pm_h, ps, pe = make_config_inputs(args.config)
-        N = z_h.shape[1]
-        prec = args.precision or {0: "fp32", 1: "fp16"}.get(args.config, "bf16")
-        # unchecked in the timed loop (no host sync per step); the status is read on every rank at the end
-        sp = ShardedPair(N, prec, dev, exchange=getattr(args, "exchange", "peer"), checked=False)
-        exchange = sp.exchange  # "nccl" if the peer mappings were refused on some rank
-        packs = []
-        for starting, p in ((True, ps), (False, pe)):
-            m = TriangleAttention(starting=starting, precision=prec).to(dev)
-            load_params(m, {k: (v.to(dev) if v is not None else None) for k, v in p.items()})
-            packs.append(m.packed_weights(sp.dt))
-        mask = pm_h[0].contiguous().to(dev)
-        z_loc = z_h[0, sp.r0:sp.r1].contiguous().to(dev)
-        # the residual stream stays in block layout across steps (the layout the exchange uses)
-        z_blk = to_blocks(z_loc, sp.P, sp.zb if exchange == "peer" else torch.empty(sp.P, sp.R, sp.R, C_IN, device=dev))
-
-        def step():  # in place: every step is the same work on the updated shard
-            sp.pair_blocks(z_blk, mask, packs[0], packs[1])
-
-        for _ in range(args.warmup):
-            step()
-        torch.cuda.synchronize()
-        dist.barrier()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        stream = torch.cuda.current_stream(dev)
         with ClockSampler(physical_gpu_index(local)) as clk:
-            dist.barrier()
-            torch.cuda.synchronize()
-            ev0.record(stream)
-            for _ in range(args.steps):
-                step()
-            ev1.record(stream)
-            torch.cuda.synchronize()
-            dist.barrier()
-        ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        step_ms = float(ms)
+            rec, sp, packs, mask, z_loc, z_h, pm_h, stream = _time_sharded_pair(
+                args.config, args, dev, make_config_inputs, layer_flops, peaks)
+        N, prec, step_ms = rec["N"], rec["precision"], rec["ms_per_step"]
         fl = layer_flops(N)
         pair_flops = 2 * fl["total"]
         value = pair_flops / (step_ms * 1e-3) / 1e12
-
-        # dominant kernel: the attention core on this rank's rows (end-layer workspace), timed alone;
-        # max over ranks
-        st = _lib.stream_handle(dev)
-        L = _lib.lib()
-        for _ in range(2):
-            _lib.check(L.triattn_core(1, N, sp.r0, sp.r1, sp.dt, sp.ws.data_ptr(), sp.ws.numel(), st))
-        ev0.record(stream)
-        for _ in range(5):
-            _lib.check(L.triattn_core(1, N, sp.r0, sp.r1, sp.dt, sp.ws.data_ptr(), sp.ws.numel(), st))
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        core = torch.tensor([ev0.elapsed_time(ev1) / 5], device=dev)
-        dist.all_reduce(core, op=dist.ReduceOp.MAX)
-        core_ms = float(core)
-        pk, pk_kind = peaks()
-        tensor_peak = pk.get("bf16_tflops", 1590.0)
-        achieved = fl["core"] * sp.R / N / (core_ms * 1e-3) / 1e12
-
         # e2e: host shard + mask copied in, shard copied out, every step; consecutive steps are
         # pipelined over two device slots (input copy / pair / output copy on three streams)
         zh = z_h[0, sp.r0:sp.r1].contiguous().pin_memory()
@@ -598,6 +634,18 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
         oh = ohs[0]
         status = torch.tensor([_lib.device_status()], device=dev)
         dist.all_reduce(status, op=dist.ReduceOp.MAX)
+        nested = None
+        if args.config == 2:
+            # the north star's scaling target is quoted at N=2048 (config 4): the same pair at the same P
+            sp.close()
+            sp = None
+            torch.cuda.empty_cache()
+            nested, sp, *_ = _time_sharded_pair(4, args, dev, make_config_inputs, layer_flops, peaks)
+            st4 = torch.tensor([_lib.device_status()], device=dev)
+            dist.all_reduce(st4, op=dist.ReduceOp.MAX)
+            nested["device_status"] = int(st4)
+            nested["metric"] = metric_name(4)
+            nested["config"] = workload_config(4, ws_n)
         if rank == 0:
             line = {
                 "metric": metric_name(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": ws_n,
@@ -606,25 +654,23 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": prec,
                 "data": "synthetic: z~N(0,1)*scale, seeded trailing-padding pair mask, seeded N(0,1/128) weights",
                 "config": workload_config(args.config, ws_n),
-                "nvlink_bytes_per_rank_per_step": sp.nvlink_bytes_per_pair(),
-                "exchange": {"peer": "peer stores from the output projection + cross-GPU barrier (CUDA IPC)",
-                             "nccl": "NCCL all_to_all_single"}[exchange],
-                "roofline": {"bound": "tensor", "kernel": "core_tc (flash attention core, this rank's rows)",
-                             "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
-                             "frac": achieved / tensor_peak, "peak_kind": f"{pk_kind} bf16 burst, per GPU",
-                             "traffic": None, "core_ms": core_ms,
-                             "algorithmic": f"F_core * R / N = {fl['core'] * sp.R / N:.4g} FLOP per launch"},
+                "nvlink_bytes_per_rank_per_step": rec["nvlink_bytes_per_rank_per_step"],
+                "exchange": rec["exchange"],
+                "roofline": rec["roofline"],
+                "cpu_baseline": {"note": "timed on rank 0 of the 1-GPU run only (the same host and workload)"},
                 "e2e": {"value": pair_flops / (float(e2e) * 1e-3) / 1e12, "unit": "TFLOP/s",
                         "ms_per_step": float(e2e), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
                         "d2h_bytes_per_step": oh.numel() * 4 * ws_n,
                         "pipelined": "input copy, pair and output copy of consecutive steps overlap (2 device slots)"},
-                "gpu_launches": args.steps * 2 * (7 if exchange == "peer" else 4),
+                "gpu_launches": rec["gpu_launches"],
                 "device_status": int(status),
                 "clocks": clk.summary(),
             }
+            if nested is not None:
+                line["config4_same_gpus"] = nested
             print(json.dumps(line), flush=True)
     finally:
-        if "sp" in locals():
+        if sp is not None:
             sp.close()
         dist.barrier()
         dist.destroy_process_group()
