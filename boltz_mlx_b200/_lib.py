@@ -25,7 +25,8 @@ EXPORTED = [
     "triattn_out_proj_vt", "triattn_peer_alloc", "triattn_peer_free", "triattn_ipc_handle", "triattn_ipc_open",
     "triattn_ipc_close", "triattn_peer_barrier", "triattn_peer_broadcast", "triattn_forward_chunked",
     "triattn_trimul_packed_bytes", "triattn_trimul_pack_weights", "triattn_trimul_workspace_bytes",
-    "triattn_trimul_forward", "triattn_trimul_forward_addln",
+    "triattn_trimul_forward", "triattn_trimul_forward_addln", "triattn_forward_fused_tb",
+    "triattn_trimul_forward_addln_tb",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -70,6 +71,8 @@ def lib() -> ctypes.CDLL:
         L.triattn_forward_chunked.argtypes = [_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _i, _vp, _sz, _vp]
         L.triattn_forward_fused.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _i, _vp, _vp, _vp, _i,
                                             _vp, _sz, _vp]
+        L.triattn_forward_fused_tb.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp, _i, _vp, _vp,
+                                               _vp, _i, _vp, _vp, _vp, _sz, _vp]
         L.triattn_mask_prep.argtypes = [_vp, _i, _i, _i, _f, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_ln_proj.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
         L.triattn_core.argtypes = [_i, _i, _i, _i, _i, _vp, _sz, _vp]
@@ -98,6 +101,8 @@ def lib() -> ctypes.CDLL:
         L.triattn_trimul_pack_weights.argtypes = [_vp] * 8 + [_i, _vp, _sz, _vp]
         L.triattn_trimul_forward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]
         L.triattn_trimul_forward_addln.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
+        L.triattn_trimul_forward_addln_tb.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                      _vp, _sz, _vp]
         for name in EXPORTED:
             if name not in ("triattn_version", "triattn_last_error_string", "triattn_packed_weights_bytes",
                             "triattn_workspace_bytes", "triattn_trimul_packed_bytes",

@@ -132,6 +132,9 @@ LayerArgs make_args(int B, int N, int starting, int row_begin, int row_end, floa
   a.xn = nullptr;
   a.ln_next_w = a.ln_next_b = nullptr;
   a.ln_out = nullptr;
+  a.tb_in = nullptr;
+  a.tb_next_w = nullptr;
+  a.tb_next = nullptr;
   return a;
 }
 
@@ -412,7 +415,21 @@ int triattn_forward_fused(const float* z, const void* xn, const float* mask, con
                           int starting, float inf, int dtype, int add_residual, float* out, int out_attn_layout,
                           const float* ln_next_w, const float* ln_next_b, void* ln_out, int ln_out_swapped,
                           void* workspace, size_t workspace_bytes, void* stream) {
+  return triattn_forward_fused_tb(z, xn, nullptr, mask, packed, B, N, starting, inf, dtype, add_residual, out,
+                                  out_attn_layout, ln_next_w, ln_next_b, ln_out, ln_out_swapped, nullptr, nullptr,
+                                  workspace, workspace_bytes, stream);
+}
+
+int triattn_forward_fused_tb(const float* z, const void* xn, const void* tb, const float* mask, const void* packed,
+                             int B, int N, int starting, float inf, int dtype, int add_residual, float* out,
+                             int out_attn_layout, const float* ln_next_w, const float* ln_next_b, void* ln_out,
+                             int ln_out_swapped, const float* tb_next_w, void* tb_next, void* workspace,
+                             size_t workspace_bytes, void* stream) {
   if (int r = check_dims(B, N, dtype)) return r;
+  if (tb && !xn) return fail(TRIATTN_EINVAL, "tb (the producer's tri bias) comes with xn, the producer's LayerNorm output");
+  if (tb && !aligned(tb, 2)) return fail(TRIATTN_EINVAL, "tb must be a 2-byte aligned device pointer");
+  if (tb_next && (!ln_out || !tb_next_w || !aligned(tb_next, 2) || !aligned(tb_next_w, 16)))
+    return fail(TRIATTN_EINVAL, "tb_next needs ln_out, a 16-byte aligned tb_next_w and a 2-byte aligned tb_next");
   if ((xn || ln_out) && dtype == DT_F32)
     return fail(TRIATTN_EUNSUPPORTED, "xn / ln_out belong to the 16-bit path (the reference's f16 pair block)");
   if (!out || !aligned(out, 16)) return fail(TRIATTN_EINVAL, "out must be a 16-byte aligned device pointer");
@@ -437,6 +454,9 @@ int triattn_forward_fused(const float* z, const void* xn, const float* mask, con
     // z's orientation seen from this layer, or with the two N axes swapped
     a.lnv = pair_view(N, ln_out_swapped ? !starting : starting, C_IN);
   }
+  a.tb_in = tb;
+  a.tb_next_w = tb_next_w;
+  a.tb_next = tb_next;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_mask_prep(a, dtype, st);
   if (e != cudaSuccess) return cuda_fail(e, "mask_prep");
@@ -496,7 +516,7 @@ int triattn_trimul_pack_weights(const float* in_w, const float* in_b, const floa
 
 static int trimul_call(const float* z, const float* mask, const void* packed, int B, int N, int outgoing, int dtype,
                        int add_residual, float* out, const float* ln_next_w, const float* ln_next_b, void* ln_out,
-                       void* workspace, size_t workspace_bytes, void* stream) {
+                       const float* tb_next_w, void* tb_next, void* workspace, size_t workspace_bytes, void* stream) {
   if (int r = check_dims(B, N, dtype)) return r;
   if ((long long)B * N * N > 2147483647LL) return fail(TRIATTN_EUNSUPPORTED, "B*N*N above 2^31 pairs");
   if (!z || !aligned(z, 16)) return fail(TRIATTN_EINVAL, "z must be a 16-byte aligned device pointer");
@@ -511,6 +531,7 @@ static int trimul_call(const float* z, const float* mask, const void* packed, in
   a.B = B; a.N = N; a.outgoing = outgoing ? 1 : 0; a.dtype = dtype; a.add_residual = add_residual ? 1 : 0;
   a.out = out; a.ws = static_cast<unsigned char*>(workspace);
   a.ln_next_w = ln_next_w; a.ln_next_b = ln_next_b; a.ln_out = ln_out;
+  a.tb_next_w = tb_next_w; a.tb_next = tb_next;
   int blas = 0;
   const char* stage = "";
   const cudaError_t e = launch_trimul(a, static_cast<cudaStream_t>(stream), &blas, &stage);
@@ -522,19 +543,29 @@ static int trimul_call(const float* z, const float* mask, const void* packed, in
 int triattn_trimul_forward(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
                            int dtype, int add_residual, float* out, void* workspace, size_t workspace_bytes,
                            void* stream) {
-  return trimul_call(z, mask, packed, B, N, outgoing, dtype, add_residual, out, nullptr, nullptr, nullptr, workspace,
-                     workspace_bytes, stream);
+  return trimul_call(z, mask, packed, B, N, outgoing, dtype, add_residual, out, nullptr, nullptr, nullptr, nullptr,
+                     nullptr, workspace, workspace_bytes, stream);
 }
 
 int triattn_trimul_forward_addln(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
                                  int dtype, float* out, const float* ln_next_w, const float* ln_next_b, void* ln_out,
                                  void* workspace, size_t workspace_bytes, void* stream) {
+  return triattn_trimul_forward_addln_tb(z, mask, packed, B, N, outgoing, dtype, out, ln_next_w, ln_next_b, ln_out,
+                                         nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int triattn_trimul_forward_addln_tb(const float* z, const float* mask, const void* packed, int B, int N, int outgoing,
+                                    int dtype, float* out, const float* ln_next_w, const float* ln_next_b,
+                                    void* ln_out, const float* tb_next_w, void* tb_next, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
   if (dtype == DT_F32) return fail(TRIATTN_EUNSUPPORTED, "trimul addln belongs to the 16-bit path");
   if (!ln_out || !aligned(ln_out, 16) || !ln_next_w || !ln_next_b || !aligned(ln_next_w, 16) ||
       !aligned(ln_next_b, 16))
     return fail(TRIATTN_EINVAL, "ln_out needs 16-byte aligned ln_out, ln_next_w and ln_next_b");
-  return trimul_call(z, mask, packed, B, N, outgoing, dtype, 1, out, ln_next_w, ln_next_b, ln_out, workspace,
-                     workspace_bytes, stream);
+  if (tb_next && (!tb_next_w || !aligned(tb_next, 2) || !aligned(tb_next_w, 16)))
+    return fail(TRIATTN_EINVAL, "tb_next needs a 16-byte aligned tb_next_w and a 2-byte aligned tb_next");
+  return trimul_call(z, mask, packed, B, N, outgoing, dtype, 1, out, ln_next_w, ln_next_b, ln_out, tb_next_w, tb_next,
+                     workspace, workspace_bytes, stream);
 }
 
 int triattn_forward_chunked(const float* z, const float* mask, const void* packed, int B, int N, int starting,

@@ -52,7 +52,7 @@ constexpr int LP_W_BYTES = NPROJ * C_IN * 2;  // 131072
 constexpr int LP_A_BYTES = TILE * C_IN * 2;   // 32768
 constexpr int LP_SMEM = LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4 + 64;
 
-template <typename T, bool XN>
+template <typename T, bool XN, bool TB>
 __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sW = smem;
@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   // caller-given LayerNorm output (16-bit, this layer's type): the LN is skipped and its bits become
   // the operand image as they are (kernel-uniform)
   constexpr bool xn_mode = XN;
+  // the producer of xn also gave this layer's tri bias (args.tb_in): the SIMT tri-bias dot is skipped
+  constexpr bool tb_given = XN && TB;
   auto load_rows = [&](int tile, float4 (&xv)[8]) {
     const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
     if constexpr (xn_mode) {
@@ -153,21 +155,14 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
       }
       // swizzled image: one row's 256 bytes are two 128-byte runs (no bank conflicts)
       *reinterpret_cast<uint2*>(sAi + sw128_off(r, 4 * lane, LP_A_BYTES / 2)) = pk;
-      // four head sums at once: exchange halves (xor 16: heads 0,1 | 2,3; xor 8: one head each), then
-      // three more butterfly steps; lane 8 hh ends with head hh's total
-      float p[HEADS];
+      // the four head sums of this row's tri bias at once; lane 8 hh ends with head hh's total
+      if constexpr (!tb_given) {
+        float p[HEADS];
 #pragma unroll
-      for (int hh = 0; hh < HEADS; ++hh) p[hh] = n0 * wb[hh].x + n1 * wb[hh].y + n2 * wb[hh].z + n3 * wb[hh].w;
-      const bool up16 = lane & 16, up8 = lane & 8;
-      float k0 = up16 ? p[2] : p[0], k1 = up16 ? p[3] : p[1];
-      k0 += __shfl_xor_sync(0xffffffffu, up16 ? p[0] : p[2], 16);
-      k1 += __shfl_xor_sync(0xffffffffu, up16 ? p[1] : p[3], 16);
-      float k = up8 ? k1 : k0;
-      k += __shfl_xor_sync(0xffffffffu, up8 ? k0 : k1, 8);
-      k += __shfl_xor_sync(0xffffffffu, k, 4);
-      k += __shfl_xor_sync(0xffffffffu, k, 2);
-      k += __shfl_xor_sync(0xffffffffu, k, 1);
-      if ((lane & 7) == 0) sB[(lane >> 3) * TILE + r] = k;
+        for (int hh = 0; hh < HEADS; ++hh) p[hh] = n0 * wb[hh].x + n1 * wb[hh].y + n2 * wb[hh].z + n3 * wb[hh].w;
+        const float k = head_sums4(p, lane);
+        if ((lane & 7) == 0) sB[(lane >> 3) * TILE + r] = k;
+      }
     }
   };
   auto issue_mma = [&](int it) {
@@ -196,15 +191,19 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
     const float* sB = sBias + (it & 1) * HEADS * TILE;
     // ---- tri-bias rows of attention row a: fp16, log2 domain, 128 x 128 block layout [k/8][q][8];
     //      one 16-byte chunk = 8 consecutive keys of one head (padded keys 0) ----
+    //      (a producer-given tri bias: fp16 [B][HEADS][N][N], element (b, hh, a, c))
     if (tid < HEADS * (TILE / 8)) {
       const int hh = tid / (TILE / 8), kg = tid % (TILE / 8);
+      const __half* tbr = tb_given ? static_cast<const __half*>(args.tb_in) + (((size_t)b * HEADS + hh) * N + a) * N : nullptr;
+      auto bias_at = [&](int r0) -> float {
+        if (c0 + r0 >= N) return 0.0f;
+        return (tb_given ? __half2float(tbr[c0 + r0]) : sB[hh * TILE + r0]) * LOG2E;
+      };
       uint32_t w[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r0 = kg * 8 + 2 * i;
-        const float v0 = c0 + r0 < N ? sB[hh * TILE + r0] * LOG2E : 0.0f;
-        const float v1 = c0 + r0 + 1 < N ? sB[hh * TILE + r0 + 1] * LOG2E : 0.0f;
-        w[i] = H16<__half>::pack(v0, v1);
+        w[i] = H16<__half>::pack(bias_at(r0), bias_at(r0 + 1));
       }
       *reinterpret_cast<uint4*>(args.ws + args.wl.off_bias + bias16_off(a, c0 + kg * 8, b, hh, args.B, NT)) =
           make_uint4(w[0], w[1], w[2], w[3]);
@@ -303,16 +302,19 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
-template <typename T, bool XN>
+template <typename T, bool XN, bool TB = false>
 static cudaError_t ln_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
-  cudaFuncSetAttribute(ln_proj_tc_kernel<T, XN>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM);
+  cudaFuncSetAttribute(ln_proj_tc_kernel<T, XN, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM);
   const int ntiles = a.wl.NT * (a.row_end - a.row_begin) * a.B;
   const int grid = ntiles < a.num_sms ? ntiles : a.num_sms;
-  ln_proj_tc_kernel<T, XN><<<grid, LP_THREADS, LP_SMEM, st>>>(a);
+  ln_proj_tc_kernel<T, XN, TB><<<grid, LP_THREADS, LP_SMEM, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_ln_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
+  if (a.xn && a.tb_in)
+    return dtype == DT_BF16 ? ln_proj_tc_launch<__nv_bfloat16, true, true>(a, st)
+                            : ln_proj_tc_launch<__half, true, true>(a, st);
   if (a.xn) return dtype == DT_BF16 ? ln_proj_tc_launch<__nv_bfloat16, true>(a, st) : ln_proj_tc_launch<__half, true>(a, st);
   return dtype == DT_BF16 ? ln_proj_tc_launch<__nv_bfloat16, false>(a, st) : ln_proj_tc_launch<__half, false>(a, st);
 }
@@ -881,7 +883,7 @@ constexpr int OP_SMEM_BODY = TILE * OP_STAGE_LD * 4;  // 67584 B: covers the two
 constexpr int OP_SMEM = OP_SMEM_BODY + 64;
 static_assert(OP_SMEM_BODY >= 65536, "staging buffer overlays the operand images");
 
-template <typename T, bool LN_NEXT, bool PERSIST>
+template <typename T, bool LN_NEXT, bool PERSIST, bool TB>
 __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs args) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
@@ -996,6 +998,10 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
     load_z(0);
     tc_fence_before();
     __syncthreads();
+    // the next tri bias from the rounded LayerNorm rows (kernel-uniform): lane 8 hh + i keeps head hh of
+    // rows 16 warp + i (tbk0) and 16 warp + 8 + i (tbk1), stored once the warp's 16 rows are done
+    constexpr bool tb_out = LN_NEXT && TB;
+    float tbk0 = 0.f, tbk1 = 0.f;
   #pragma unroll 1
     for (int h = 0; h < 2; ++h) {
       if (h == 1) load_z(1);
@@ -1017,6 +1023,34 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
           pk.x = H16<T>::pack(d0 * rstd * lw.x + lb.x, d1 * rstd * lw.y + lb.y);
           pk.y = H16<T>::pack(d2 * rstd * lw.z + lb.z, d3 * rstd * lw.w + lb.w);
           *(reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(args.ln_out) + row_off(args.lnv, r)) + lane) = pk;
+          if constexpr (tb_out) {
+            // reference _LN_EPI_TB (kernels_nax3.py:104-143): fp32 sums of the rounded LayerNorm values
+            const float2 a01 = H16<T>::unpack(pk.x), a23 = H16<T>::unpack(pk.y);
+            float p[HEADS];
+  #pragma unroll
+            for (int hh = 0; hh < HEADS; ++hh) {
+              const float4 w = __ldg(reinterpret_cast<const float4*>(args.tb_next_w + hh * C_IN) + lane);
+              p[hh] = a01.x * w.x + a01.y * w.y + a23.x * w.z + a23.y * w.w;
+            }
+            const float k = head_sums4(p, lane);
+            if ((lane & 7) == i) {
+              if (h == 0) tbk0 = k;
+              else tbk1 = k;
+            }
+          }
+        }
+      }
+    }
+    if constexpr (tb_out) {
+      // fp16 [B][HEADS][N][N], the pair index of ln_out (a dense view: row0 = 0, no block table)
+      const int i = lane & 7, hh = lane >> 3;
+  #pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = 16 * warp + 8 * h + i;
+        if (ct * TILE + r < N) {
+          const long long pidx = (row_off(args.lnv, r) - b * args.lnv.s_batch) / C_IN;
+          reinterpret_cast<__half*>(args.tb_next)[((long long)b * HEADS + hh) * N * N + pidx] =
+              __float2half_rn(h ? tbk1 : tbk0);
         }
       }
     }
@@ -1037,21 +1071,24 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
   if (warp == 0) tmem_dealloc(tbase, 128);
 }
 
-template <typename T, bool LN_NEXT>
+template <typename T, bool LN_NEXT, bool TB = false>
 static cudaError_t out_proj_tc_launch(const LayerArgs& a, cudaStream_t st) {
   const int n_tiles = a.wl.NT * (a.row_end - a.row_begin) * a.B;
   if (a.ov.tab || a.lnv.tab) {  // output blocks on peer GPUs: persistent, three resident CTAs per SM
-    cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
+    cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT, true, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
     const int grid = n_tiles < 3 * a.num_sms ? n_tiles : 3 * a.num_sms;
-    out_proj_tc_kernel<T, LN_NEXT, true><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
+    out_proj_tc_kernel<T, LN_NEXT, true, TB><<<grid, OP_THREADS, OP_SMEM, st>>>(a);
   } else {
-    cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
-    out_proj_tc_kernel<T, LN_NEXT, false><<<n_tiles, OP_THREADS, OP_SMEM, st>>>(a);
+    cudaFuncSetAttribute(out_proj_tc_kernel<T, LN_NEXT, false, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, OP_SMEM);
+    out_proj_tc_kernel<T, LN_NEXT, false, TB><<<n_tiles, OP_THREADS, OP_SMEM, st>>>(a);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_out_proj_tc(const LayerArgs& a, int dtype, cudaStream_t st) {
+  if (a.ln_out && a.tb_next)
+    return dtype == DT_BF16 ? out_proj_tc_launch<__nv_bfloat16, true, true>(a, st)
+                            : out_proj_tc_launch<__half, true, true>(a, st);
   if (a.ln_out)
     return dtype == DT_BF16 ? out_proj_tc_launch<__nv_bfloat16, true>(a, st) : out_proj_tc_launch<__half, true>(a, st);
   return dtype == DT_BF16 ? out_proj_tc_launch<__nv_bfloat16, false>(a, st) : out_proj_tc_launch<__half, false>(a, st);

@@ -141,8 +141,11 @@ struct TrimulArgs {
   const float* z; const float* mask; const unsigned char* packed;
   int B, N, outgoing, dtype, add_residual;
   float* out; unsigned char* ws;
-  // optional (16-bit modes): the next module's LayerNorm of out, written in the layer's type
+  // optional (16-bit modes): the next module's LayerNorm of out, written in the layer's type, and from
+  // its rounded values the next triangle attention's tri bias (fp32 weights [HEADS][128] -> fp16
+  // [B][HEADS][N][N], pairs in ln_out's order)
   const float* ln_next_w; const float* ln_next_b; void* ln_out;
+  const float* tb_next_w; void* tb_next;
 };
 
 // Byte offset of tri-bias element (q, k) of head h, batch b on the 16-bit path.
@@ -196,7 +199,29 @@ struct LayerArgs {
   const void* xn; View xnv;
   const float* ln_next_w; const float* ln_next_b;
   void* ln_out; View lnv;
+  // optional (16-bit path, with xn): this layer's tri bias computed by the producer of xn, fp16
+  // [B][HEADS][N][N] in natural units and the layer's attention orientation (the projection then skips
+  // its own tri-bias dot); and, with ln_out, the next triangle attention's tri bias from the rounded
+  // ln_out rows (fp32 weights [HEADS][128] -> fp16 [B][HEADS][N][N], pairs in ln_out's order)
+  const void* tb_in;
+  const float* tb_next_w; void* tb_next;
 };
+
+// Four per-head sums of one row spread over a warp (lane: partial p[h] of its channels).  Halves are
+// exchanged first (xor 16: heads 0,1 | 2,3; xor 8: one head each), then three butterfly steps; every
+// lane of group h (lanes 8h .. 8h + 7) ends with head h's total.
+__device__ __forceinline__ float head_sums4(const float (&p)[HEADS], int lane) {
+  const bool up16 = lane & 16, up8 = lane & 8;
+  float k0 = up16 ? p[2] : p[0], k1 = up16 ? p[3] : p[1];
+  k0 += __shfl_xor_sync(0xffffffffu, up16 ? p[0] : p[2], 16);
+  k1 += __shfl_xor_sync(0xffffffffu, up16 ? p[1] : p[3], 16);
+  float k = up8 ? k1 : k0;
+  k += __shfl_xor_sync(0xffffffffu, up8 ? k0 : k1, 8);
+  k += __shfl_xor_sync(0xffffffffu, k, 4);
+  k += __shfl_xor_sync(0xffffffffu, k, 2);
+  k += __shfl_xor_sync(0xffffffffu, k, 1);
+  return k;
+}
 
 // launchers (return cudaGetLastError())
 cudaError_t launch_pack_weights(const float* ln_w, const float* ln_b, const float* w_q, const float* w_k,

@@ -342,12 +342,12 @@ constexpr int TT_STAGE_LD = TM_D + 4;
 constexpr int TT_SMEM_BODY = TILE * TT_STAGE_LD * 4;  // 67584 B, covers the two 32 KB operand images
 constexpr int TT_SMEM = TT_SMEM_BODY + 2 * 2 * TILE * 4 + 64;
 
-template <typename T, bool LN_NEXT>
+template <typename T, bool LN_NEXT, bool TB>
 __global__ void __launch_bounds__(TT_THREADS, 3)
     tm_tail_tc_kernel(const float* __restrict__ o, const unsigned char* __restrict__ packed, const T* __restrict__ gout,
                       const float* z, float* out, long long npairs, long long nn, int add_residual,
                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, T* __restrict__ ln_out,
-                      int* status) {
+                      const float* __restrict__ tb_w, __half* __restrict__ tb_out, int* status) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sA = smem;
   unsigned char* sW = smem + 32768;
@@ -453,6 +453,10 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     nw = reinterpret_cast<const float4*>(ln_w)[lane];
     nb = reinterpret_cast<const float4*>(ln_b)[lane];
   }
+  // the next triangle attention's tri bias from the rounded LayerNorm rows: lane 8 hh + i keeps head hh
+  // of rows 16 warp + i (tbk0) and 16 warp + 8 + i (tbk1)
+  constexpr bool tb_on = LN_NEXT && TB;
+  float tbk0 = 0.f, tbk1 = 0.f;
 #pragma unroll 4
   for (int i = 0; i < 16; ++i) {
     const int r = 16 * warp + i;
@@ -471,8 +475,37 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
       const float d0 = res.x - mean, d1 = res.y - mean, d2 = res.z - mean, d3 = res.w - mean;
       const float var = tm_warp_sum((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3)) * (1.0f / TM_D);
       const float rs = rsqrtf(var + LN_EPS);
-      Ew<T>::st4(ln_out + p * TM_D + 4 * lane, make_float4(d0 * rs * nw.x + nb.x, d1 * rs * nw.y + nb.y,
-                                                         d2 * rs * nw.z + nb.z, d3 * rs * nw.w + nb.w));
+      const float4 ln4 = make_float4(d0 * rs * nw.x + nb.x, d1 * rs * nw.y + nb.y, d2 * rs * nw.z + nb.z,
+                                     d3 * rs * nw.w + nb.w);
+      const uint2 pk = make_uint2(H16<T>::pack(ln4.x, ln4.y), H16<T>::pack(ln4.z, ln4.w));
+      *reinterpret_cast<uint2*>(ln_out + p * TM_D + 4 * lane) = pk;
+      if constexpr (tb_on) {
+        // reference _LN_EPI_TB (kernels_nax3.py:104-143): fp32 sums of the rounded LayerNorm values
+        const float2 h01 = H16<T>::unpack(pk.x), h23 = H16<T>::unpack(pk.y);
+        float pp[HEADS];
+#pragma unroll
+        for (int hh = 0; hh < HEADS; ++hh) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(tb_w + hh * TM_D) + lane);
+          pp[hh] = h01.x * w.x + h01.y * w.y + h23.x * w.z + h23.y * w.w;
+        }
+        const float k = head_sums4(pp, lane);
+        if ((lane & 7) == (i & 7)) {
+          if (i < 8) tbk0 = k;
+          else tbk1 = k;
+        }
+      }
+    }
+  }
+  if constexpr (tb_on) {
+    // fp16 [B][HEADS][N][N]: pair p of batch bb -> (bb * HEADS + hh) * nn + (p - bb * nn)
+    const int hh = lane >> 3;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const long long p = p0 + 16 * warp + 8 * h + (lane & 7);
+      if (p < npairs) {
+        const long long bb = p / nn;
+        tb_out[(bb * HEADS + hh) * nn + (p - bb * nn)] = __float2half_rn(h ? tbk1 : tbk0);
+      }
     }
   }
   __syncthreads();
@@ -624,16 +657,21 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   if constexpr (sizeof(T) == 2) {
     *stage = "tail";
     const int grid = (int)((P + TILE - 1) / TILE);
-    if (a.ln_out) {
-      cudaFuncSetAttribute(tm_tail_tc_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
-      tm_tail_tc_kernel<T, true><<<grid, TT_THREADS, TT_SMEM, st>>>(
+    if (a.ln_out && a.tb_next) {
+      cudaFuncSetAttribute(tm_tail_tc_kernel<T, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+      tm_tail_tc_kernel<T, true, true><<<grid, TT_THREADS, TT_SMEM, st>>>(
           o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, a.ln_next_w, a.ln_next_b,
-          reinterpret_cast<T*>(a.ln_out), device_status_ptr());
+          reinterpret_cast<T*>(a.ln_out), a.tb_next_w, reinterpret_cast<__half*>(a.tb_next), device_status_ptr());
+    } else if (a.ln_out) {
+      cudaFuncSetAttribute(tm_tail_tc_kernel<T, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+      tm_tail_tc_kernel<T, true, false><<<grid, TT_THREADS, TT_SMEM, st>>>(
+          o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, a.ln_next_w, a.ln_next_b,
+          reinterpret_cast<T*>(a.ln_out), nullptr, nullptr, device_status_ptr());
     } else {
-      cudaFuncSetAttribute(tm_tail_tc_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
-      tm_tail_tc_kernel<T, false><<<grid, TT_THREADS, TT_SMEM, st>>>(o, a.packed, gout, a.z, a.out, P, nn,
-                                                                      a.add_residual, nullptr, nullptr, nullptr,
-                                                                      device_status_ptr());
+      cudaFuncSetAttribute(tm_tail_tc_kernel<T, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+      tm_tail_tc_kernel<T, false, false><<<grid, TT_THREADS, TT_SMEM, st>>>(
+          o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, nullptr, nullptr, nullptr, nullptr, nullptr,
+          device_status_ptr());
     }
     return cudaGetLastError();
   }

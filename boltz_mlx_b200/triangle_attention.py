@@ -234,20 +234,25 @@ class TriangleAttention(nn.Module):
         xn = this module's LayerNorm output (ending node: already transposed), then the output projection,
         the residual add and the next module's LayerNorm in the output kernel's epilogue.
 
-        `ln_next`: a LayerNorm module (weight, bias; eps 1e-5).  `tb` (this module's tri bias precomputed
-        by the producer of xn) is accepted and not needed: the projection kernel derives the tri bias
-        from xn itself.  `w_tb` [H, c_in]: also return the next module's tri bias LN_out . w_tb^T as
-        [B, H, Q, K] (the layout of the reference's tb), from the 16-bit LayerNorm output."""
-        del tb
-        z_new, ln_out = self._run_fused(z, mask, xn, add_residual=True, keep_t=False, ln_next=ln_next,
-                                        trans_out=trans_out)
+        `ln_next`: a LayerNorm module (weight, bias; eps 1e-5).  `tb` [B, H, N, N]: this module's tri bias
+        computed by the producer of xn (laid out like xn; fp16 in natural units), used by the projection
+        instead of its own LN . w_b dot (attention.py:128-147).  `w_tb` [H, c_in] (the next triangle
+        attention's tb_weight16()): also return that module's tri bias, computed in the output kernel's
+        epilogue from the rounded 16-bit LayerNorm rows (fp32 sums, one rounding to fp16), as
+        [B, H, Q, K] in ln_out's layout (the reference's PAIRTB, kernels_nax3.py:104-143)."""
+        z_new, ln_out, tb_next = self._run_fused(z, mask, xn, add_residual=True, keep_t=False, ln_next=ln_next,
+                                                 trans_out=trans_out, tb=tb, w_tb=w_tb)
         if w_tb is None:
             return z_new, ln_out
-        w = w_tb.to(device=ln_out.device, dtype=ln_out.dtype)
-        tb_next = (ln_out @ w.t()).permute(0, 3, 1, 2).contiguous()
         return z_new, ln_out, tb_next
 
-    def _run_fused(self, x, mask, xn, *, add_residual: bool, keep_t: bool, ln_next=None, trans_out: bool = False):
+    def tb_weight16(self) -> torch.Tensor:
+        """The tri-bias projection weight [H, c_in] rounded to fp16, as the reference passes it to the
+        producer's f16_addln(w_tb=...) (attention.py:158-164)."""
+        return self.linear.weight.detach().to(torch.float16)
+
+    def _run_fused(self, x, mask, xn, *, add_residual: bool, keep_t: bool, ln_next=None, trans_out: bool = False,
+                   tb=None, w_tb=None):
         self._check_geometry()
         if not x.is_cuda:
             raise RuntimeError("TriangleAttention (B200) needs CUDA tensors; there is no CPU path")
@@ -275,16 +280,32 @@ class TriangleAttention(nn.Module):
             lw = ln_next.weight.detach().to(device=z.device, dtype=torch.float32).contiguous()
             lb = ln_next.bias.detach().to(device=z.device, dtype=torch.float32).contiguous()
             ln_out = torch.empty(z.shape, dtype=t16, device=z.device)
+        H = self.no_heads
+        if tb is not None:
+            if xn is None:
+                raise ValueError("tb (the producer's tri bias) comes with xn, the producer's LayerNorm output")
+            if tuple(tb.shape) != (B, H, N, N):
+                raise ValueError(f"tb must be [B, H, N, N] = {(B, H, N, N)}, got {tuple(tb.shape)}")
+            tb = tb.to(device=z.device, dtype=torch.float16).contiguous()
+        wt, tb_next = None, None
+        if w_tb is not None:
+            if ln_next is None:
+                raise ValueError("w_tb needs ln_next: the next tri bias is computed from the next LayerNorm's output")
+            if tuple(w_tb.shape) != (H, self.c_in):
+                raise ValueError(f"w_tb must be [H, c_in] = {(H, self.c_in)}, got {tuple(w_tb.shape)}")
+            wt = w_tb.detach().to(device=z.device, dtype=torch.float32).contiguous()
+            tb_next = torch.empty(B, H, N, N, dtype=torch.float16, device=z.device)
         packed = self.packed_weights(dtype)
         nbytes = _lib.workspace_bytes(B, N, N, dtype)
         ws = self._ws.get(nbytes, z.device)
         out_attn = int(keep_t and not self.starting)
-        _lib.check(_lib.lib().triattn_forward_fused(
-            z.data_ptr(), _lib.ptr(xn), _lib.ptr(m), packed.data_ptr(), B, N, int(self.starting), float(self.inf),
-            dtype, int(add_residual), out.data_ptr(), out_attn, _lib.ptr(lw), _lib.ptr(lb), _lib.ptr(ln_out),
-            int(trans_out), ws.data_ptr(), ws.numel(), _lib.stream_handle(z.device)))
-        self._fused_keepalive = (xn, m, lw, lb)  # inputs stay alive until the (asynchronous) launch has run
-        return out, ln_out
+        _lib.check(_lib.lib().triattn_forward_fused_tb(
+            z.data_ptr(), _lib.ptr(xn), _lib.ptr(tb), _lib.ptr(m), packed.data_ptr(), B, N, int(self.starting),
+            float(self.inf), dtype, int(add_residual), out.data_ptr(), out_attn, _lib.ptr(lw), _lib.ptr(lb),
+            _lib.ptr(ln_out), int(trans_out), _lib.ptr(wt), _lib.ptr(tb_next), ws.data_ptr(), ws.numel(),
+            _lib.stream_handle(z.device)))
+        self._fused_keepalive = (xn, tb, m, lw, lb, wt)  # inputs stay alive until the (asynchronous) launch has run
+        return out, ln_out, tb_next
 
     def forward_residual(self, z: torch.Tensor, mask: Optional[torch.Tensor] = None, *,
                          inplace: bool = False, chunk_size: Optional[int] = None) -> torch.Tensor:

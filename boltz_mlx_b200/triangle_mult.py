@@ -104,8 +104,10 @@ class _TriangleMultiplication(nn.Module):
         """(z + self(z), ln_next(z + self(z)) 16-bit[, next tri bias]) as the reference's f16_addln
         (triangular_mult.py:93-115): the output gate, the residual add and the next module's LayerNorm in
         the tail kernel.  16-bit precisions only.  `xn` (norm_in(z), precomputed) is accepted and
-        recomputed from z.  `w_tb` [H, 128]: also return the next triangle attention's tri bias
-        LN_out . w_tb^T as [B, H, N, N]."""
+        recomputed from z.  `w_tb` [H, 128] (the next triangle attention's tb_weight16()): also return
+        that module's tri bias, computed in the tail kernel's epilogue from the rounded 16-bit LayerNorm
+        rows (fp32 sums, one rounding to fp16), as [B, H, N, N] (the reference's PAIRTB,
+        kernels_nax3.py:104-143)."""
         del xn
         if not z.is_cuda:
             raise RuntimeError("TriangleMultiplication (B200) needs CUDA tensors; there is no CPU path")
@@ -126,15 +128,23 @@ class _TriangleMultiplication(nn.Module):
         lb = ln_next.bias.detach().to(device=zc.device, dtype=torch.float32).contiguous()
         out = torch.empty_like(zc)
         ln_out = torch.empty(zc.shape, dtype=t16, device=zc.device)
+        wt, tb_next = None, None
+        if w_tb is not None:
+            if w_tb.dim() != 2 or w_tb.shape[1] != self.dim:
+                raise ValueError(f"w_tb must be [H, {self.dim}], got {tuple(w_tb.shape)}")
+            if w_tb.shape[0] != 4:
+                raise _lib.TriAttnUnsupported(_lib.EUNSUPPORTED, "the tail kernel writes the tri bias of 4 heads")
+            wt = w_tb.detach().to(device=zc.device, dtype=torch.float32).contiguous()
+            tb_next = torch.empty(B, 4, N, N, dtype=torch.float16, device=zc.device)
         packed = self.packed_weights(dtype)
         ws = self._ws.get(_lib.lib().triattn_trimul_workspace_bytes(B, N, dtype), zc.device)
-        _lib.check(_lib.lib().triattn_trimul_forward_addln(
+        _lib.check(_lib.lib().triattn_trimul_forward_addln_tb(
             zc.data_ptr(), _lib.ptr(m), packed.data_ptr(), B, N, int(self.outgoing), dtype, out.data_ptr(),
-            lw.data_ptr(), lb.data_ptr(), ln_out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(zc.device)))
+            lw.data_ptr(), lb.data_ptr(), ln_out.data_ptr(), _lib.ptr(wt), _lib.ptr(tb_next), ws.data_ptr(), ws.numel(),
+            _lib.stream_handle(zc.device)))
         if w_tb is None:
             return out, ln_out
-        w = w_tb.to(device=ln_out.device, dtype=ln_out.dtype)
-        return out, ln_out, (ln_out @ w.t()).permute(0, 3, 1, 2).contiguous()
+        return out, ln_out, tb_next
 
 
 class TriangleMultiplicationOutgoing(_TriangleMultiplication):

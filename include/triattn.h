@@ -150,6 +150,22 @@ TRIATTN_API int triattn_forward_fused(const float* z, const void* xn, const floa
                                       int out_attn_layout, const float* ln_next_w, const float* ln_next_b,
                                       void* ln_out, int ln_out_swapped, void* workspace, size_t workspace_bytes,
                                       void* stream);
+/* triattn_forward_fused with the pair block's tri-bias hand-over <- the reference's tb / w_tb arguments
+ *   of f16_addln (attention.py:170-190, consumed by _f16_core at :128-147; kernels.py:1537-1539) and the
+ *   PAIRTB LayerNorm epilogue (_LN_EPI_TB, kernels_nax3.py:104-143):
+ *   tb        : NULL, or (with xn) this layer's tri bias as computed by the producer of xn, fp16
+ *               [B][4][N][N] in natural units, laid out like xn (the layer's attention orientation);
+ *               the projection then takes it instead of its own LN . w_b dot.
+ *   tb_next_w : fp32 [4][128], the next triangle attention's tri-bias weight; with ln_out and tb_next,
+ *   tb_next   : fp16 [B][4][N][N] <- sum_c ln_out[pair][c] * tb_next_w[h][c] over the ROUNDED 16-bit
+ *               ln_out values, fp32 sums, one rounding; pairs in ln_out's order (ln_out_swapped included).
+ * Every other argument as triattn_forward_fused, which is this call with tb = tb_next_w = tb_next = NULL. */
+TRIATTN_API int triattn_forward_fused_tb(const float* z, const void* xn, const void* tb, const float* mask,
+                                         const void* packed, int B, int N, int starting, float inf, int dtype,
+                                         int add_residual, float* out, int out_attn_layout, const float* ln_next_w,
+                                         const float* ln_next_b, void* ln_out, int ln_out_swapped,
+                                         const float* tb_next_w, void* tb_next, void* workspace,
+                                         size_t workspace_bytes, void* stream);
 
 /* ---- strided-view stages (row-sharded / column-blocked pair tensors) ------------------------
  * The _v variants address an attention-oriented VIEW of a pair tensor instead of a dense [B][N][N]
@@ -259,6 +275,15 @@ TRIATTN_API int triattn_trimul_forward_addln(const float* z, const float* mask, 
                                              int outgoing, int dtype, float* out, const float* ln_next_w,
                                              const float* ln_next_b, void* ln_out, void* workspace,
                                              size_t workspace_bytes, void* stream);
+/* triattn_trimul_forward_addln that also writes the next triangle attention's tri bias <- the
+ * reference's f16_addln(..., w_tb=...) of the tri-mult (kernels.py:1537, PAIRTB epilogue
+ * kernels_nax3.py:104-143): tb_next fp16 [B][4][N][N] = sum_c ln_out[pair][c] * tb_next_w[h][c]
+ * (tb_next_w fp32 [4][128]) over the rounded ln_out values, pairs in ln_out's (z's) order. */
+TRIATTN_API int triattn_trimul_forward_addln_tb(const float* z, const float* mask, const void* packed, int B, int N,
+                                                int outgoing, int dtype, float* out, const float* ln_next_w,
+                                                const float* ln_next_b, void* ln_out, const float* tb_next_w,
+                                                void* tb_next, void* workspace, size_t workspace_bytes,
+                                                void* stream);
 
 /* ---- allocation-free layer ----------------------------------------------------------------
  * No counterpart in the reference.  triattn_forward without a workspace argument, for callers that

@@ -78,8 +78,74 @@ def test_f16_addln(precision, starting):
     w_tb = 0.1 * torch.randn(4, 128, generator=g).cuda()
     z2, ln_t, tb = m.f16_addln(z, mask, xn, ln_next, trans_out=True, w_tb=w_tb)
     assert torch.equal(z2, z_new) and torch.equal(ln_t, ln_out.transpose(1, 2))
-    tb_ref = (ln_t @ w_tb.to(ln_t.dtype).t()).permute(0, 3, 1, 2)
-    assert tb.shape == (1, 4, N, N) and torch.equal(tb, tb_ref)
+    # the next tri bias from the output kernel's epilogue (PAIRTB): fp32 sums of the rounded ln_out values,
+    # one rounding to fp16, in ln_out's (here transposed) layout
+    tb_ref = (ln_t.float() @ w_tb.t()).permute(0, 3, 1, 2)
+    assert tb.shape == (1, 4, N, N) and tb.dtype == torch.float16
+    assert ((tb.float() - tb_ref).abs() <= 2.0 ** -11 * tb_ref.abs() + 1e-5).all()
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+@pytest.mark.parametrize("starting", [True, False])
+def test_producer_tri_bias_is_consumed(precision, starting):
+    """tb given with xn (attention.py:128-147): the projection takes the producer's tri bias instead of
+    its own dot.  The producer's fp16 tb of the same xn gives the same layer up to the bias rounding;
+    a tb of zeros gives the layer without a tri bias."""
+    N = 150
+    g = torch.Generator().manual_seed(17)
+    z = torch.randn(1, N, N, 128, generator=g).cuda()
+    mask = rand_mask(g, 1, N).cuda()
+    p = make_params(6, gate_bias=1.0)
+    m = module(p, starting, precision)
+    ln_next = torch.nn.LayerNorm(128).cuda()
+    xn = _ln16(z, m.layer_norm, starting, precision)
+    tb = (xn.float() @ m.linear.weight.detach().float().t()).permute(0, 3, 1, 2).to(torch.float16).contiguous()
+    z_own, ln_own = m.f16_addln(z, mask, xn, ln_next)
+    z_tb, ln_tb = m.f16_addln(z, mask, xn, ln_next, tb=tb)
+    d = (z_tb - z_own).abs()
+    assert float(d.max()) < 2e-2 and float(d.mean()) < 1e-3
+    # with a zero tri bias the result is the layer without one (oracle with w_b = 0)
+    p0 = dict(p, w_b=torch.zeros_like(p["w_b"]))
+    z_0, _ = m.f16_addln(z, mask, xn, ln_next, tb=torch.zeros_like(tb))
+    ref = tri_attention_ref(z.cpu().double(), mask.cpu().double(),
+                            {k: (v.double() if v is not None else None) for k, v in p0.items()},
+                            starting=starting, dtype=torch.float64)
+    assert_parity(z_0 - z, ref, precision, "tb = 0")
+    with pytest.raises(ValueError):
+        m.f16_addln(z, mask, None, ln_next, tb=tb)
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+def test_tri_bias_handover_chain_matches_oracle(precision):
+    """The reference's f16 pair block with the tri bias handed over (kernels.py:1537-1539): tri_mul_in
+    -> (ln_start, tb_start) -> start layer on them -> (ln_end transposed, tb_end) -> end layer on them.
+    Each layer's update is checked against the float64 oracle applied to that layer's actual input."""
+    from boltz_mlx_b200 import TriangleMultiplicationIncoming, load_trimul_params
+    from oracle.trimul_ref import make_params as tm_params, trimul_ref
+
+    N = 128
+    g = torch.Generator().manual_seed(29)
+    z = torch.randn(1, N, N, 128, generator=g)
+    mask = rand_mask(g, 1, N)
+    pm, ps, pe = tm_params(31), make_params(32, gate_bias=1.0), make_params(33, gate_bias=1.0)
+    tmi = load_trimul_params(TriangleMultiplicationIncoming(128, precision=precision).cuda(), pm)
+    start, end = module(ps, True, precision), module(pe, False, precision)
+    ln_last = torch.nn.LayerNorm(128).cuda()
+    zc, mc = z.cuda(), mask.cuda()
+    z1, xn1, tb1 = tmi.f16_addln(zc, mc, None, start.layer_norm, w_tb=start.tb_weight16())
+    z2, xn2, tb2 = start.f16_addln(z1, mc, xn1, end.layer_norm, trans_out=True, tb=tb1, w_tb=end.tb_weight16())
+    z3, _ = end.f16_addln(z2, mc, xn2, ln_last, tb=tb2)
+    d = lambda p: {k: (v.double() if v is not None else None) for k, v in p.items()}
+    m64 = mask.double()
+    z1_64, z2_64 = z1.cpu().double(), z2.cpu().double()
+    # the tri-mult layer to its own tolerance (max error relative to the largest output, mean absolute)
+    from tests.test_gpu_trimul import assert_parity as assert_trimul_parity
+    assert_trimul_parity(z1 - zc, trimul_ref(z.double(), m64, d(pm), outgoing=False, dtype=torch.float64), precision,
+                         "tri_mul_in")
+    assert_parity(z2 - z1, tri_attention_ref(z1_64, m64, d(ps), starting=True, dtype=torch.float64), precision,
+                  "start layer on the handed-over xn, tb")
+    assert_parity(z3 - z2, tri_attention_ref(z2_64, m64, d(pe), starting=False, dtype=torch.float64), precision,
+                  "end layer on the handed-over xn, tb")
 
 
 @pytest.mark.parametrize("precision", ["bf16", "fp16"])
