@@ -82,6 +82,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Wait, for at most `ns` nanoseconds and whatever the status word says, for a phase that copies still
+// in flight complete (a kernel leaving after an error drains its own copies this way).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_timer_ns() - t0 > ns) return;
+}
+
 // Wait for the phase with the given parity to complete.  Bounded: returns false (and records
 // `code` in *status) after TRIATTN_WAIT_NS, or soon after another thread has recorded an error.
 // try_wait parks the warp in hardware between polls; the status word and the global timer are
@@ -112,6 +120,17 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           smem_u32(smem_dst)),
       "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Tiled tensor copy (TMA) global -> shared of one box of a 3-D tensor map at coordinates (x, y, z), x the
+// innermost (contiguous) dimension; completion counted on `bar`.  No multicast.  x * element size must
+// be a multiple of 16 bytes; elements outside the tensor read as zero.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -279,6 +298,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>((1024u >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+// MN-major operand in the 128-byte swizzled layout (what a TMA box of 64 MN values x K rows with
+// 128-byte swizzle leaves in shared memory): one K index per 128-byte row holding 64 consecutive MN
+// values, the 16-byte chunk index XORed with k % 8; 8-row atoms of 1024 B along K (SBO); MN blocks of
+// 64 values `lbo` bytes apart (LBO).  A K step of 16 advances the start by 2048 B.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((1024u >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
   d |= 2ull << 61;

@@ -97,8 +97,9 @@ struct Workspace {
 // ---- triangle multiplication (outgoing / incoming edges) -----------------------------------------
 // packed weights: fp32 section: in_w, in_b, out_w, out_b [128 each]; W1 = p_in | g_in | g_out
 // [640][128]; p_out [128][128].  16-bit section (16-bit modes): W1 and p_out in the layer's type,
-// row-major (cuBLAS operands), and the p_in | g_in rows (512 x 128) and p_out (128 x 128) once more as
-// K-major no-swizzle UMMA operand images (img_off) for the fused projection and tail kernels.
+// row-major, and as K-major no-swizzle UMMA operand images (img_off) for the fused projection and
+// tail kernels: img_pg = 640 rows p_in[0:128] | g_in[0:128] | p_in[128:256] | g_in[128:256] | g_out
+// (the a half, the b half, then the output gate), img_po = p_out (128 x 128).
 constexpr int TM_D = 128;
 constexpr int TM_W1 = 5 * TM_D;  // 640 = p_in (256) | g_in (256) | g_out (128)
 struct TrimulPacked {
@@ -109,30 +110,36 @@ struct TrimulPacked {
   static constexpr size_t w1_16 = align_up(f32_end, 256);
   static constexpr size_t p_out_16 = w1_16 + (size_t)TM_W1 * TM_D * 2;
   static constexpr size_t img_pg = align_up(p_out_16 + (size_t)TM_D * TM_D * 2, 1024);
-  static constexpr size_t img_po = img_pg + (size_t)4 * TM_D * TM_D * 2;  // p_out as a 128 x 128 image
+  static constexpr size_t img_po = img_pg + (size_t)5 * TM_D * TM_D * 2;  // p_out as a 128 x 128 image
   static constexpr size_t end16 = img_po + (size_t)TM_D * TM_D * 2;
   static constexpr size_t bytes(int dtype) { return dtype == DT_F32 ? align_up(f32_end, 256) : align_up(end16, 256); }
 };
-// workspace of one call over P = B*N*N pairs (es = element size of the layer's type):
-//   xn  [P][128]      LayerNorm-in output (es); later norm_out's output (same place)
+// workspace of one call over P = B*N*N pairs (es = element size of the layer's type).  The channel
+// planes of a, b and o are N rows of Np elements (16-bit modes: Np = N rounded up to 8, so that every
+// row starts 16-byte aligned for the contraction's TMA loads; fp32 mode: Np = N).
+//   xn  fp32 mode: [P][128] LayerNorm-in output, later norm_out's output (same place); 16-bit: none
 //   h   fp32 mode: [P][640] projection p | g | g_out; 16-bit modes: [P][128] g_out only (the fused
-//       projection kernel gates a and b in its epilogue and never writes p, g)
-//   ab  [2][B][128][N][N]  gated + masked a, b, channel-major (es); later p_out's output [P][128] fp32
-//   o   [B][128][N][N]     contraction output, fp32, channel-major
-//   blas                   32 MiB scratch handed to cuBLAS
+//       projection kernel gates a and b in its epilogue and writes the output gate's projection)
+//   ab  [2][B][128][N][Np]  gated + masked a, b, channel-major (es); fp32 mode: later p_out's output
+//       [P][128] fp32
+//   o   [B][128][N][Np]     contraction output, fp32, channel-major
+//   blas                    fp32 mode: 32 MiB scratch handed to cuBLAS
 struct TrimulWorkspace {
   size_t off_xn, off_h, off_ab, off_o, off_blas, total;
+  int Np;
   static constexpr size_t BLAS_BYTES = 32ull << 20;
   __host__ __device__ static TrimulWorkspace make(int B, int N, int dtype) {
     TrimulWorkspace w{};
-    const size_t P = (size_t)B * N * N, es = dtype == DT_F32 ? 4 : 2, A = 256;
+    const bool f32 = dtype == DT_F32;
+    w.Np = f32 ? N : (N + 7) / 8 * 8;
+    const size_t P = (size_t)B * N * N, Pp = (size_t)B * N * w.Np, es = f32 ? 4 : 2, A = 256;
     size_t o = 0;
-    w.off_xn = o; o = align_up(o + P * TM_D * es, A);
-    w.off_h = o; o = align_up(o + P * (dtype == DT_F32 ? TM_W1 : TM_D) * es, A);
-    const size_t ab = 2 * P * TM_D * es, po = P * TM_D * 4;
+    w.off_xn = o; o = align_up(o + (f32 ? P * TM_D * es : 0), A);
+    w.off_h = o; o = align_up(o + P * (f32 ? TM_W1 : TM_D) * es, A);
+    const size_t ab = 2 * Pp * TM_D * es, po = f32 ? P * TM_D * 4 : 0;
     w.off_ab = o; o = align_up(o + (ab > po ? ab : po), A);
-    w.off_o = o; o = align_up(o + P * TM_D * 4, A);
-    w.off_blas = o; o = align_up(o + BLAS_BYTES, A);
+    w.off_o = o; o = align_up(o + Pp * TM_D * 4, A);
+    w.off_blas = o; o = align_up(o + (f32 ? BLAS_BYTES : 0), A);
     w.total = o;
     return w;
   }

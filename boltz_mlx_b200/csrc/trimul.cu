@@ -23,9 +23,12 @@
 // per warp); the three GEMMs are plain library GEMMs.
 #include <cstdint>
 #include <cublas_v2.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <mutex>
+#include <type_traits>
 
 #include "sm100.cuh"
 #include "triattn_internal.cuh"
@@ -184,33 +187,38 @@ __global__ void __launch_bounds__(256) tm_out_kernel(const float* z, const float
   }
 }
 
-// ---- F1 (16-bit modes): fused LayerNorm-in + [p_in | g_in] projection + gate/mask epilogue --------
-// Persistent, one CTA per SM (512 threads), the 128 KB operand image of [p_in | g_in] loaded once.
+// ---- F1 (16-bit modes): fused LayerNorm-in + [p_in | g_in | g_out] projection + gate/mask epilogue --
+// Persistent, one CTA per SM (512 threads), the 160 KB operand image of [p_in | g_in | g_out] loaded once.
 // Tile = 128 consecutive pairs.  Per tile: LayerNorm (warp w: pairs 8w..8w+7, lane: channels
-// 4 lane..+3) into a 128-byte-swizzled operand image and, as a by-product, xn to global memory (the
-// g_out GEMM's operand); UMMA D[128 x 512] = xn [p_in | g_in]^T in two N = 256 halves (p | g, TMEM
-// columns 0..255 | 256..511); epilogue: warp (quad, tt) takes TMEM lanes 32 quad.. and channels
-// 64 tt.. of a|b, a = p sigmoid(g) m, written channel-major (a warp's 32 lanes are 32 consecutive
-// pairs of one channel row: 64-byte runs).  The LayerNorm of tile it + 1 runs while the MMA of tile it
-// executes (two operand images), as in the attention projection kernel.
+// 4 lane..+3) into a 128-byte-swizzled operand image; UMMA D[128 x 512] = xn [p_a | g_a | p_b | g_b]^T in
+// two N = 256 halves (TMEM columns 0..255 | 256..511, one commit each); epilogue in three phases, warp
+// (quad, tt) taking TMEM lanes 32 quad.. and channels 32 tt..: (a) a = p_a sigmoid(g_a) m into the
+// channel-major a planes (a warp's 32 lanes are 32 consecutive pairs of one channel row: 64-byte runs);
+// once every warp has read the a columns, the output gate's projection xn g_out^T (N = 128) runs into
+// columns 0..127 while (b) gates b; (c) the output gate's projection (pre-sigmoid, 16-bit) into g_out
+// [P][128] for the tail.  The LayerNorm of tile it + 1 runs while the MMA of tile it executes (two
+// operand images), as in the attention projection kernel.
 constexpr int TP_THREADS = 512;
-constexpr int TP_W_BYTES = 4 * TM_D * TM_D * 2;  // 512 x 128 16-bit image
+constexpr int TP_W_BYTES = 5 * TM_D * TM_D * 2;  // 640 x 128 16-bit image
 constexpr int TP_A_BYTES = TILE * TM_D * 2;      // one 128-pair LayerNorm image
 constexpr int TP_SMEM = TP_W_BYTES + 2 * TP_A_BYTES + 64;
+static_assert(TP_SMEM <= 232448, "projection shared memory");
 
 template <typename T>
 __global__ void __launch_bounds__(TP_THREADS, 1)
     tm_proj_tc_kernel(const float* __restrict__ z, const float* __restrict__ mask, const unsigned char* __restrict__ packed,
-                      T* __restrict__ xn, T* __restrict__ ab, long long npairs, long long nn, int B, int* status) {
+                      T* __restrict__ gout, T* __restrict__ ab, long long npairs, int N, int Np, int B, int* status) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sW = smem;
   unsigned char* sA = smem + TP_W_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TP_W_BYTES + 2 * TP_A_BYTES);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
   uint64_t* bar_w = bars;
-  uint64_t* bar_mma = bars + 1;
+  uint64_t* bar_mma = bars + 1;   // [3]: a half, b half, output gate
+  uint64_t* bar_adone = bars + 4;  // every warp has read the a half's columns
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long ntiles = (npairs + TILE - 1) / TILE;
+  const long long nn = (long long)N * N, plane = (long long)N * Np;
   const float* Pf = reinterpret_cast<const float*>(packed);
   if ((smem_u32(sA) & 1023u) != 0) {  // the swizzled image needs a 1024-byte aligned base (CTA-uniform)
     if (tid == 0) atomicCAS(status, 0, (int)DEV_BAD_ALIGN);
@@ -218,7 +226,8 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   }
   if (tid == 0) {
     mbar_init(bar_w, 1);
-    mbar_init(bar_mma, 1);
+    for (int i = 0; i < 3; ++i) mbar_init(bar_mma + i, 1);
+    mbar_init(bar_adone, TP_THREADS / 32);
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(tslot, 512);
@@ -239,12 +248,11 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       xv[i] = p < npairs ? __ldcs(reinterpret_cast<const float4*>(z + p * TM_D) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
-  auto ln_tile = [&](int it, long long tile, const float4 (&xv)[8]) {
+  auto ln_tile = [&](int it, const float4 (&xv)[8]) {
     unsigned char* sAi = sA + (it & 1) * TP_A_BYTES;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = warp * 8 + i;
-      const long long p = tile * TILE + r;
       const float4 v = xv[i];
       const float mean = tm_warp_sum((v.x + v.y) + (v.z + v.w)) * (1.0f / TM_D);
       const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
@@ -253,25 +261,28 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       const uint2 pk = make_uint2(H16<T>::pack(d0 * rs * lw.x + lb.x, d1 * rs * lw.y + lb.y),
                                   H16<T>::pack(d2 * rs * lw.z + lb.z, d3 * rs * lw.w + lb.w));
       *reinterpret_cast<uint2*>(sAi + sw128_off(r, 4 * lane, TP_A_BYTES / 2)) = pk;
-      if (p < npairs) *reinterpret_cast<uint2*>(xn + p * TM_D + 4 * lane) = pk;
+    }
+  };
+  // rows [row0, row0 + N) of the weight image against image it & 1 into TMEM column col0 (one thread)
+  auto mma_rows = [&](int it, int row0, int col0, auto n_const) {
+    constexpr int NN = decltype(n_const)::value;
+    unsigned char* sAi = sA + (it & 1) * TP_A_BYTES;
+    constexpr uint32_t idesc = make_idesc_f16(128, NN, H16<T>::is_bf16, 0, 0);
+#pragma unroll
+    for (int ks = 0; ks < TM_D / 16; ++ks) {
+      const uint64_t ad = smem_desc_sw128(smem_u32(sAi) + (ks / 4) * (TP_A_BYTES / 2) + (ks % 4) * 32);
+      const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + (row0 / 8) * (16 * TM_D) + ks * 256, 128, 16 * TM_D);
+      umma_ss(tbase + col0, ad, bd, idesc, ks > 0 ? 1u : 0u);
     }
   };
   auto issue_mma = [&](int it) {
     if (tid == 0) {
-      unsigned char* sAi = sA + (it & 1) * TP_A_BYTES;
       if (it == 0) mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
       tc_fence_after();
-      constexpr uint32_t idesc = make_idesc_f16(128, 256, H16<T>::is_bf16, 0, 0);
-#pragma unroll
-      for (int nh = 0; nh < 2; ++nh) {
-#pragma unroll
-        for (int ks = 0; ks < TM_D / 16; ++ks) {
-          const uint64_t ad = smem_desc_sw128(smem_u32(sAi) + (ks / 4) * (TP_A_BYTES / 2) + (ks % 4) * 32);
-          const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * TM_D);
-          umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
-        }
-      }
-      umma_commit(bar_mma);
+      mma_rows(it, 0, 0, std::integral_constant<int, 256>{});  // p_a | g_a
+      umma_commit(bar_mma + 0);
+      mma_rows(it, 256, 256, std::integral_constant<int, 256>{});  // p_b | g_b
+      umma_commit(bar_mma + 1);
     }
   };
   auto epilogue = [&](int it, long long tile) {
@@ -280,23 +291,59 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
     const bool valid = p < npairs;
     const float m = valid ? (mask ? mask[p] : 1.0f) : 0.0f;
     const long long bb = valid ? p / nn : 0, pp = valid ? p - bb * nn : 0;
-    mbar_wait(bar_mma, it & 1, status, DEV_TIMEOUT_MMA);
+    const long long prow = pp / N, pcol = pp - prow * N;
+    // channels 32 tt .. 32 tt + 31 of a (sel 0) or b (sel 1): p at TMEM column colp + c, g at colg + c
+    auto gate = [&](int sel, int colp, int colg) {
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int c = 32 * tt + 16 * h2;
+        uint32_t pv[16], gv[16];
+        tmem_ld16(tmem_addr(tbase, quad * 32, colp + c), pv);
+        tmem_ld16(tmem_addr(tbase, quad * 32, colg + c), gv);
+        tmem_ld_wait();
+        tmem_regs_ready(pv);
+        tmem_regs_ready(gv);
+        if (valid) {
+          T* dst = ab + ((long long)(sel * B + bb) * TM_D + c) * plane + prow * Np + pcol;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            dst[j * plane] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid(__uint_as_float(gv[j])) * m);
+        }
+      }
+    };
+    mbar_wait(bar_mma + 0, it & 1, status, DEV_TIMEOUT_MMA);
     __syncwarp();
     tc_fence_after();
-#pragma unroll 1
-    for (int q4 = 0; q4 < 4; ++q4) {
-      const int c0 = 64 * tt + 16 * q4;  // channel of a | b (0..255)
-      uint32_t pv[16], gv[16];
-      tmem_ld16(tmem_addr(tbase, quad * 32, c0), pv);
-      tmem_ld16(tmem_addr(tbase, quad * 32, 256 + c0), gv);
+    gate(0, 0, 128);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_adone);
+    if (tid == 0) {  // the a columns are free: the output gate's projection into columns 0..127
+      mbar_wait(bar_adone, it & 1, status, DEV_TIMEOUT_SYNC);
+      tc_fence_after();
+      mma_rows(it, 512, 0, std::integral_constant<int, 128>{});
+      umma_commit(bar_mma + 2);
+    }
+    mbar_wait(bar_mma + 1, it & 1, status, DEV_TIMEOUT_MMA);
+    __syncwarp();
+    tc_fence_after();
+    gate(1, 256, 384);
+    mbar_wait(bar_mma + 2, it & 1, status, DEV_TIMEOUT_MMA);
+    __syncwarp();
+    tc_fence_after();
+    {
+      uint32_t gv[32];
+      tmem_ld32(tmem_addr(tbase, quad * 32, 32 * tt), gv);
       tmem_ld_wait();
-      tmem_regs_ready(pv);
       tmem_regs_ready(gv);
       if (valid) {
-        T* dst = ab + ((long long)((c0 >> 7) * B + bb) * TM_D + (c0 & 127)) * nn + pp;
+        uint4* dst = reinterpret_cast<uint4*>(gout + p * TM_D + 32 * tt);
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          dst[j * nn] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid(__uint_as_float(gv[j])) * m);
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(H16<T>::pack(__uint_as_float(gv[8 * q + 0]), __uint_as_float(gv[8 * q + 1])),
+                              H16<T>::pack(__uint_as_float(gv[8 * q + 2]), __uint_as_float(gv[8 * q + 3])),
+                              H16<T>::pack(__uint_as_float(gv[8 * q + 4]), __uint_as_float(gv[8 * q + 5])),
+                              H16<T>::pack(__uint_as_float(gv[8 * q + 6]), __uint_as_float(gv[8 * q + 7])));
       }
     }
   };
@@ -304,7 +351,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   long long tile = blockIdx.x;
   if (tile < ntiles) {
     load_rows(tile, xv);
-    ln_tile(0, tile, xv);
+    ln_tile(0, xv);
     if (tile + gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
     fence_proxy_async_smem();
     __syncthreads();
@@ -313,7 +360,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
     const long long nxt = tile + gridDim.x;
     if (nxt < ntiles) {
-      ln_tile(it + 1, nxt, xv);  // overlaps the MMA of this tile
+      ln_tile(it + 1, xv);  // overlaps the MMA of this tile
       if (nxt + gridDim.x < ntiles) load_rows(nxt + gridDim.x, xv);
       fence_proxy_async_smem();
     }
@@ -323,6 +370,158 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
     tc_fence_after();
     if (nxt < ntiles) issue_mma(it + 1);
   }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+// ---- G2 (16-bit modes): the per-channel contraction on the tensor cores ---------------------------
+// o[pl][i][j] = sum_k A[i][k] B[j][k] for every plane pl = (batch, channel) (triangular_mult.py:43-47):
+//   outgoing  A[i][k] = a[pl][i][k], B[j][k] = b[pl][j][k]  (K-major operands: k contiguous)
+//   incoming  A[i][k] = a[pl][k][i], B[j][k] = b[pl][k][j]  (MN-major operands: i / j contiguous)
+// a, b: [planes][N][Np] 16-bit, read by TMA through 3-D tensor maps (x = column, y = row, z = plane;
+// 128-byte swizzle; zero fill past N, so ragged edges and the K tail need no padding in memory).
+// o: fp32 [planes][N][Np].  Persistent, one CTA per SM, 192 threads: warp 0 lane 0 issues the TMA
+// loads, warp 1 lane 0 the MMAs, warps 2..5 are the epilogue (TMEM lane quadrant = warp % 4).  Tile =
+// 128 x 256 outputs of one plane (UMMA M = 128, N = 256, fp32 accumulation), K in blocks of 64 through
+// a ring of 4 stages of 48 KB; two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
+// overlap the main loop of the next.  Tiles are numbered plane-major (then row block, then column
+// block), so the CTAs running at the same time share a plane's a and b in L2.
+constexpr int CT_BM = 128, CT_BN = 256, CT_BK = 64, CT_STAGES = 4;
+constexpr int CT_A_BYTES = CT_BM * CT_BK * 2;  // 16 KB
+constexpr int CT_B_BYTES = CT_BN * CT_BK * 2;  // 32 KB
+constexpr int CT_STAGE = CT_A_BYTES + CT_B_BYTES;
+constexpr int CT_THREADS = 192;
+constexpr int CT_SMEM = 1024 + CT_STAGES * CT_STAGE + 256;  // + alignment slack + barriers
+static_assert(CT_SMEM <= 232448, "contraction shared memory");
+
+template <typename T, bool MN>
+__global__ void __launch_bounds__(CT_THREADS, 1)
+    tm_contract_tc_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                          float* __restrict__ o, int N, int Np, int planes, int* status) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-aligned stages
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + CT_STAGES * CT_STAGE);  // [STAGES] loads landed
+  uint64_t* empty = full + CT_STAGES;                                          // [STAGES] MMAs done reading
+  uint64_t* acc_full = empty + CT_STAGES;                                      // [2] accumulator complete
+  uint64_t* acc_empty = acc_full + 2;                                          // [2] accumulator read out
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mtn = (N + CT_BM - 1) / CT_BM, ntn = (N + CT_BN - 1) / CT_BN, nk = (N + CT_BK - 1) / CT_BK;
+  const int ntiles = planes * mtn * ntn;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < CT_STAGES; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  auto coords = [&](int t, int& pl, int& m0, int& n0) {
+    const int r = t / ntn;
+    n0 = (t - r * ntn) * CT_BN;
+    pl = r / mtn;
+    m0 = (r - pl * mtn) * CT_BM;
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      int it = 0;  // k blocks issued over all tiles
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        int pl, m0, n0;
+        coords(t, pl, m0, n0);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % CT_STAGES;
+          mbar_wait(empty + st, ((it / CT_STAGES) & 1) ^ 1, status, DEV_TIMEOUT_MMA);
+          unsigned char* sa = smem + st * CT_STAGE;
+          unsigned char* sb = sa + CT_A_BYTES;
+          mbar_arrive_expect_tx(full + st, CT_STAGE);
+          const int k0 = kb * CT_BK;
+          if constexpr (!MN) {
+            tma_load_3d(sa, &tma, k0, m0, pl, full + st);  // 128 rows x 64 k
+            tma_load_3d(sb, &tmb, k0, n0, pl, full + st);  // 256 rows x 64 k
+          } else {
+#pragma unroll
+            for (int q = 0; q < CT_BM / 64; ++q) tma_load_3d(sa + q * 8192, &tma, m0 + 64 * q, k0, pl, full + st);
+#pragma unroll
+            for (int q = 0; q < CT_BN / 64; ++q) tma_load_3d(sb + q * 8192, &tmb, n0 + 64 * q, k0, pl, full + st);
+          }
+        }
+      }
+      // copies still in flight after an error: wait (bounded) for the last load of every stage
+      for (int st = 0; st < CT_STAGES && st < it; ++st) {
+        const int last = it - 1 - ((it - 1 - st) % CT_STAGES);
+        mbar_wait_drain(full + st, (last / CT_STAGES) & 1, 200000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      constexpr uint32_t idesc = make_idesc_f16(CT_BM, CT_BN, H16<T>::is_bf16, MN ? 1 : 0, MN ? 1 : 0);
+      int it = 0, tl = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+        const int acc = tl & 1;
+        mbar_wait(acc_empty + acc, ((tl >> 1) & 1) ^ 1, status, DEV_TIMEOUT_MMA);
+        tc_fence_after();
+        const uint32_t d = tbase + acc * CT_BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % CT_STAGES;
+          mbar_wait(full + st, (it / CT_STAGES) & 1, status, DEV_TIMEOUT_TMA);
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + st * CT_STAGE), sb = sa + CT_A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < CT_BK / 16; ++ks) {
+            const uint64_t ad = MN ? smem_desc_sw128_mn(sa + ks * 2048, 8192) : smem_desc_sw128(sa + ks * 32);
+            const uint64_t bd = MN ? smem_desc_sw128_mn(sb + ks * 2048, 8192) : smem_desc_sw128(sb + ks * 32);
+            umma_ss(d, ad, bd, idesc, (kb | ks) ? 1u : 0u);
+          }
+          umma_commit(empty + st);  // the stage is free once these MMAs have read it
+        }
+        umma_commit(acc_full + acc);
+      }
+    }
+  } else {
+    // ---- epilogue: rows m0 + 32 q + lane, fp32 stores of 32 columns at a time ----
+    const int q = warp & 3;
+    int tl = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+      int pl, m0, n0;
+      coords(t, pl, m0, n0);
+      const int acc = tl & 1;
+      mbar_wait(acc_full + acc, (tl >> 1) & 1, status, DEV_TIMEOUT_MMA);
+      __syncwarp();
+      tc_fence_after();
+      const int i = m0 + 32 * q + lane;
+      float* orow = o + ((long long)pl * N + (i < N ? i : 0)) * Np;
+#pragma unroll 1
+      for (int c = 0; c < CT_BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem_addr(tbase + acc * CT_BN, 32 * q, 32 * c), v);
+        tmem_ld_wait();
+        tmem_regs_ready(v);
+        const int j0 = n0 + 32 * c;
+        if (i < N) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            if (j0 + e < Np)
+              *reinterpret_cast<float4*>(orow + j0 + e) = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                                                                      __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty + acc);
+    }
+  }
+  tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
@@ -345,7 +544,7 @@ constexpr int TT_SMEM = TT_SMEM_BODY + 2 * 2 * TILE * 4 + 64;
 template <typename T, bool LN_NEXT, bool TB>
 __global__ void __launch_bounds__(TT_THREADS, 3)
     tm_tail_tc_kernel(const float* __restrict__ o, const unsigned char* __restrict__ packed, const T* __restrict__ gout,
-                      const float* z, float* out, long long npairs, long long nn, int add_residual,
+                      const float* z, float* out, long long npairs, int N, int Np, int add_residual,
                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, T* __restrict__ ln_out,
                       const float* __restrict__ tb_w, __half* __restrict__ tb_out, int* status) {
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -377,11 +576,13 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     const int r = tid & (TILE - 1), half = tid >> 7;
     const long long p = p0 + r;
     const bool valid = p < npairs;
+    const long long nn = (long long)N * N, plane = (long long)N * Np;
     const long long bb = valid ? p / nn : 0, pp = valid ? p - bb * nn : 0;
-    const float* src = o + (bb * TM_D + 64 * half) * nn + pp;
+    const long long prow = pp / N;
+    const float* src = o + (bb * TM_D + 64 * half) * plane + prow * Np + (pp - prow * N);
     float v[64];
 #pragma unroll
-    for (int d = 0; d < 64; ++d) v[d] = valid ? __ldcs(src + d * nn) : 0.0f;
+    for (int d = 0; d < 64; ++d) v[d] = valid ? __ldcs(src + d * plane) : 0.0f;
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int d = 0; d < 64; d += 2) { s0 += v[d]; s1 += v[d + 1]; }
@@ -503,7 +704,7 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     for (int h = 0; h < 2; ++h) {
       const long long p = p0 + 16 * warp + 8 * h + (lane & 7);
       if (p < npairs) {
-        const long long bb = p / nn;
+        const long long nn = (long long)N * N, bb = p / nn;
         tb_out[(bb * HEADS + hh) * nn + (p - bb * nn)] = __float2half_rn(h ? tbk1 : tbk0);
       }
     }
@@ -526,8 +727,9 @@ __global__ void tm_pack_kernel(const float* in_w, const float* in_b, const float
     f[TrimulPacked::w1 / 4 + i] = v;
     if (with16) {
       reinterpret_cast<T*>(packed + TrimulPacked::w1_16)[i] = static_cast<T>(v);
-      if (r < 4 * TM_D)
-        reinterpret_cast<T*>(packed + TrimulPacked::img_pg)[img_off(r, i % TM_D, TM_D) / 2] = static_cast<T>(v);
+      // image row of W1 row r: p_in[0:128] | g_in[0:128] | p_in[128:256] | g_in[128:256] | g_out
+      const int ri = r < 2 * TM_D ? (r < TM_D ? r : r + TM_D) : (r < 4 * TM_D ? (r < 3 * TM_D ? r - TM_D : r) : r);
+      reinterpret_cast<T*>(packed + TrimulPacked::img_pg)[img_off(ri, i % TM_D, TM_D) / 2] = static_cast<T>(v);
       if (r < TM_D)
         reinterpret_cast<T*>(packed + TrimulPacked::img_po)[img_off(r, i % TM_D, TM_D) / 2] = static_cast<T>(p_out[i]);
     }
@@ -566,27 +768,104 @@ cublasHandle_t blas_handle(int* err) {
   return handles[dev];
 }
 
-template <typename T>
-cudaDataType_t cuda_type();
-template <>
-cudaDataType_t cuda_type<float>() { return CUDA_R_32F; }
-template <>
-cudaDataType_t cuda_type<__half>() { return CUDA_R_16F; }
-template <>
-cudaDataType_t cuda_type<__nv_bfloat16>() { return CUDA_R_16BF; }
-
 int grid_for(long long work, int per_block, int cap) {
   const long long g = (work + per_block - 1) / per_block;
   return (int)(g < cap ? (g < 1 ? 1 : g) : cap);
 }
 
+// TMA descriptor of the a or b planes: [planes][N][Np] 16-bit, x = column (contiguous), y = row,
+// z = plane, box (64, box_y, 1), 128-byte swizzle, zero fill outside [0, N) x [0, N).
+// cuTensorMapEncodeTiled comes from the driver through the runtime's entry-point query (no libcuda link).
+cudaError_t encode_planes(CUtensorMap* m, const void* base, bool bf16, int N, int Np, int planes, int box_y) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)N, (cuuint64_t)planes};
+  const cuuint64_t strides[2] = {(cuuint64_t)Np * 2, (cuuint64_t)N * Np * 2};
+  const cuuint32_t box[3] = {64u, (cuuint32_t)box_y, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// 16-bit modes: F1 projection -> G2 contraction -> T1 tail, all hand-written tcgen05 kernels.
 template <typename T>
-cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, const char** stage) {
+cudaError_t trimul_run16(const TrimulArgs& a, cudaStream_t st, const char** stage) {
+  const TrimulWorkspace wl = TrimulWorkspace::make(a.B, a.N, a.dtype);
+  const int N = a.N, Np = wl.Np, planes = a.B * TM_D;
+  const long long P = (long long)a.B * N * N;
+  T* gout = reinterpret_cast<T*>(a.ws + wl.off_h);
+  T* ab = reinterpret_cast<T*>(a.ws + wl.off_ab);
+  float* o = reinterpret_cast<float*>(a.ws + wl.off_o);
+  int* status = device_status_ptr();
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e;
+
+  *stage = "fused projection";
+  cudaFuncSetAttribute(tm_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM);
+  const long long ptiles = (P + TILE - 1) / TILE;
+  tm_proj_tc_kernel<T><<<(int)(ptiles < sms ? ptiles : sms), TP_THREADS, TP_SMEM, st>>>(a.z, a.mask, a.packed, gout,
+                                                                                       ab, P, N, Np, a.B, status);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+  *stage = "contraction";
+  CUtensorMap ma, mb;
+  const bool bf16 = a.dtype == DT_BF16;
+  // outgoing: K-major boxes of 64 k x 128 (a) / 256 (b) rows; incoming: MN-major boxes of 64 columns x 64 k
+  if ((e = encode_planes(&ma, ab, bf16, N, Np, planes, a.outgoing ? CT_BM : CT_BK)) != cudaSuccess) return e;
+  if ((e = encode_planes(&mb, ab + (size_t)planes * N * Np, bf16, N, Np, planes, a.outgoing ? CT_BN : CT_BK)) !=
+      cudaSuccess)
+    return e;
+  const int ctiles = planes * ((N + CT_BM - 1) / CT_BM) * ((N + CT_BN - 1) / CT_BN);
+  const int cgrid = ctiles < sms ? ctiles : sms;
+  if (a.outgoing) {
+    cudaFuncSetAttribute(tm_contract_tc_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
+    tm_contract_tc_kernel<T, false><<<cgrid, CT_THREADS, CT_SMEM, st>>>(ma, mb, o, N, Np, planes, status);
+  } else {
+    cudaFuncSetAttribute(tm_contract_tc_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
+    tm_contract_tc_kernel<T, true><<<cgrid, CT_THREADS, CT_SMEM, st>>>(ma, mb, o, N, Np, planes, status);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+  *stage = "tail";
+  const int grid = (int)((P + TILE - 1) / TILE);
+  if (a.ln_out && a.tb_next) {
+    cudaFuncSetAttribute(tm_tail_tc_kernel<T, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+    tm_tail_tc_kernel<T, true, true><<<grid, TT_THREADS, TT_SMEM, st>>>(
+        o, a.packed, gout, a.z, a.out, P, N, Np, a.add_residual, a.ln_next_w, a.ln_next_b,
+        reinterpret_cast<T*>(a.ln_out), a.tb_next_w, reinterpret_cast<__half*>(a.tb_next), status);
+  } else if (a.ln_out) {
+    cudaFuncSetAttribute(tm_tail_tc_kernel<T, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+    tm_tail_tc_kernel<T, true, false><<<grid, TT_THREADS, TT_SMEM, st>>>(
+        o, a.packed, gout, a.z, a.out, P, N, Np, a.add_residual, a.ln_next_w, a.ln_next_b,
+        reinterpret_cast<T*>(a.ln_out), nullptr, nullptr, status);
+  } else {
+    cudaFuncSetAttribute(tm_tail_tc_kernel<T, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
+    tm_tail_tc_kernel<T, false, false><<<grid, TT_THREADS, TT_SMEM, st>>>(
+        o, a.packed, gout, a.z, a.out, P, N, Np, a.add_residual, nullptr, nullptr, nullptr, nullptr, nullptr, status);
+  }
+  return cudaGetLastError();
+}
+
+// fp32 mode: every step in fp32, the three GEMMs as plain cuBLAS fp32 GEMMs (no TF32).
+cudaError_t trimul_run32(const TrimulArgs& a, cudaStream_t st, int* blas_status, const char** stage) {
+  using T = float;
   const TrimulWorkspace wl = TrimulWorkspace::make(a.B, a.N, a.dtype);
   const long long nn = (long long)a.N * a.N, P = (long long)a.B * nn;
   const float* pf = reinterpret_cast<const float*>(a.packed);
-  const T* w1 = reinterpret_cast<const T*>(a.packed + (sizeof(T) == 4 ? TrimulPacked::w1 : TrimulPacked::w1_16));
-  const T* wpo = reinterpret_cast<const T*>(a.packed + (sizeof(T) == 4 ? TrimulPacked::p_out : TrimulPacked::p_out_16));
+  const T* w1 = reinterpret_cast<const T*>(a.packed + TrimulPacked::w1);
+  const T* wpo = reinterpret_cast<const T*>(a.packed + TrimulPacked::p_out);
   T* xn = reinterpret_cast<T*>(a.ws + wl.off_xn);
   T* h = reinterpret_cast<T*>(a.ws + wl.off_h);
   T* ab = reinterpret_cast<T*>(a.ws + wl.off_ab);
@@ -595,21 +874,11 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-
   cudaError_t e;
-  if constexpr (sizeof(T) == 2) {
-    *stage = "fused projection";
-    cudaFuncSetAttribute(tm_proj_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM);
-    const long long ntiles = (P + TILE - 1) / TILE;
-    tm_proj_tc_kernel<T><<<(int)(ntiles < sms ? ntiles : sms), TP_THREADS, TP_SMEM, st>>>(
-        a.z, a.mask, a.packed, xn, ab, P, nn, a.B, device_status_ptr());
-  } else {
-    *stage = "layernorm_in";
-    tm_ln_in_kernel<T><<<grid_for(P, 8, sms * 16), 256, 0, st>>>(a.z, pf + TrimulPacked::in_w / 4,
-                                                                  pf + TrimulPacked::in_b / 4, xn, P);
-  }
+  *stage = "layernorm_in";
+  tm_ln_in_kernel<T><<<grid_for(P, 8, sms * 16), 256, 0, st>>>(a.z, pf + TrimulPacked::in_w / 4,
+                                                                pf + TrimulPacked::in_b / 4, xn, P);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-
   int herr = 0;
   cublasHandle_t hb = blas_handle(&herr);
   if (!hb) {
@@ -620,26 +889,20 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   cublasStatus_t s = cublasSetStream(hb, st);
   if (s == CUBLAS_STATUS_SUCCESS) s = cublasSetWorkspace(hb, a.ws + wl.off_blas, TrimulWorkspace::BLAS_BYTES);
   if (s == CUBLAS_STATUS_SUCCESS) s = cublasSetMathMode(hb, CUBLAS_DEFAULT_MATH);  // fp32 stays fp32 (no TF32)
-  const cudaDataType_t tt = cuda_type<T>();
   const float one = 1.0f, zero = 0.0f;
-  // G1, row-major out [P][n] = xn [P][128] . W^T (column-major: out^T = W . xn^T).  16-bit: W = g_out
-  // rows only (a, b come gated from F1); fp32: W = p_in | g_in | g_out, then K2 gates.
-  const int n1 = sizeof(T) == 2 ? TM_D : TM_W1;
-  const T* w1g = sizeof(T) == 2 ? w1 + (size_t)4 * TM_D * TM_D : w1;
+  // G1, row-major h [P][640] = xn [P][128] . (p_in | g_in | g_out)^T (column-major: h^T = W . xn^T)
   if (s == CUBLAS_STATUS_SUCCESS) {
     *stage = "projection GEMM";
-    s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, n1, (int)P, TM_D, &one, w1g, tt, TM_D, xn, tt, TM_D, &zero, h, tt,
-                     n1, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, TM_W1, (int)P, TM_D, &one, w1, CUDA_R_32F, TM_D, xn, CUDA_R_32F, TM_D,
+                     &zero, h, CUDA_R_32F, TM_W1, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   }
   if (s != CUBLAS_STATUS_SUCCESS) {
     *blas_status = (int)s;
     return cudaErrorUnknown;
   }
-  if constexpr (sizeof(T) == 4) {
-    *stage = "gate";
-    tm_gate_kernel<T><<<(int)((P + TM_GP - 1) / TM_GP), 256, 0, st>>>(h, a.mask, ab, P, nn, a.B);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
+  *stage = "gate";
+  tm_gate_kernel<T><<<(int)((P + TM_GP - 1) / TM_GP), 256, 0, st>>>(h, a.mask, ab, P, nn, a.B);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
   // G2, per (batch, channel), row-major N x N matrices (column-major views are their transposes):
   //   outgoing o = a . b^T   ->  o^T = b . a^T   (op(b) = T on b^T, op(a^T) = N)
   //   incoming o = a^T . b   ->  o^T = b^T . a   (op(b^T) = N, op(a) = T on a^T)
@@ -647,33 +910,11 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   const T* am = ab;
   const T* bm = ab + (long long)a.B * TM_D * nn;
   s = cublasGemmStridedBatchedEx(hb, a.outgoing ? CUBLAS_OP_T : CUBLAS_OP_N, a.outgoing ? CUBLAS_OP_N : CUBLAS_OP_T,
-                                 a.N, a.N, a.N, &one, bm, tt, a.N, nn, am, tt, a.N, nn, &zero, o, CUDA_R_32F, a.N, nn,
-                                 a.B * TM_D, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+                                 a.N, a.N, a.N, &one, bm, CUDA_R_32F, a.N, nn, am, CUDA_R_32F, a.N, nn, &zero, o,
+                                 CUDA_R_32F, a.N, nn, a.B * TM_D, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   if (s != CUBLAS_STATUS_SUCCESS) {
     *blas_status = (int)s;
     return cudaErrorUnknown;
-  }
-  const T* gout = sizeof(T) == 2 ? h : h + 4 * TM_D;  // [P][128] g_out, or the g_out columns of h [P][640]
-  if constexpr (sizeof(T) == 2) {
-    *stage = "tail";
-    const int grid = (int)((P + TILE - 1) / TILE);
-    if (a.ln_out && a.tb_next) {
-      cudaFuncSetAttribute(tm_tail_tc_kernel<T, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
-      tm_tail_tc_kernel<T, true, true><<<grid, TT_THREADS, TT_SMEM, st>>>(
-          o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, a.ln_next_w, a.ln_next_b,
-          reinterpret_cast<T*>(a.ln_out), a.tb_next_w, reinterpret_cast<__half*>(a.tb_next), device_status_ptr());
-    } else if (a.ln_out) {
-      cudaFuncSetAttribute(tm_tail_tc_kernel<T, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
-      tm_tail_tc_kernel<T, true, false><<<grid, TT_THREADS, TT_SMEM, st>>>(
-          o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, a.ln_next_w, a.ln_next_b,
-          reinterpret_cast<T*>(a.ln_out), nullptr, nullptr, device_status_ptr());
-    } else {
-      cudaFuncSetAttribute(tm_tail_tc_kernel<T, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TT_SMEM);
-      tm_tail_tc_kernel<T, false, false><<<grid, TT_THREADS, TT_SMEM, st>>>(
-          o, a.packed, gout, a.z, a.out, P, nn, a.add_residual, nullptr, nullptr, nullptr, nullptr, nullptr,
-          device_status_ptr());
-    }
-    return cudaGetLastError();
   }
   *stage = "layernorm_out";
   tm_ln_out_kernel<T><<<(int)((P + TM_LP - 1) / TM_LP), 256, 0, st>>>(o, pf + TrimulPacked::out_w / 4,
@@ -681,14 +922,14 @@ cudaError_t trimul_run(const TrimulArgs& a, cudaStream_t st, int* blas_status, c
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   // G3 (row-major y [P][128] = norm_out(o) [P][128] . p_out^T), fp32 out
   *stage = "p_out GEMM";
-  s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, TM_D, (int)P, TM_D, &one, wpo, tt, TM_D, xn, tt, TM_D, &zero, y,
-                   CUDA_R_32F, TM_D, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, TM_D, (int)P, TM_D, &one, wpo, CUDA_R_32F, TM_D, xn, CUDA_R_32F, TM_D,
+                   &zero, y, CUDA_R_32F, TM_D, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   if (s != CUBLAS_STATUS_SUCCESS) {
     *blas_status = (int)s;
     return cudaErrorUnknown;
   }
   *stage = "output gate";
-  tm_out_kernel<T><<<grid_for(P * 32, 256, sms * 16), 256, 0, st>>>(a.z, y, gout, n1, a.out, P * 32,
+  tm_out_kernel<T><<<grid_for(P * 32, 256, sms * 16), 256, 0, st>>>(a.z, y, h + 4 * TM_D, TM_W1, a.out, P * 32,
                                                                      a.add_residual);
   return cudaGetLastError();
 }
@@ -708,9 +949,9 @@ cudaError_t launch_trimul_pack(const float* in_w, const float* in_b, const float
 
 cudaError_t launch_trimul(const TrimulArgs& a, cudaStream_t st, int* blas_status, const char** stage) {
   *blas_status = 0;
-  if (a.dtype == DT_F32) return trimul_run<float>(a, st, blas_status, stage);
-  if (a.dtype == DT_BF16) return trimul_run<__nv_bfloat16>(a, st, blas_status, stage);
-  return trimul_run<__half>(a, st, blas_status, stage);
+  if (a.dtype == DT_F32) return trimul_run32(a, st, blas_status, stage);
+  if (a.dtype == DT_BF16) return trimul_run16<__nv_bfloat16>(a, st, stage);
+  return trimul_run16<__half>(a, st, stage);
 }
 
 }  // namespace triattn

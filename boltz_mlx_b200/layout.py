@@ -186,17 +186,21 @@ def trimul_packed_bytes(dtype: int) -> int:
     w1_16 = align(f32_end)
     p_out_16 = w1_16 + TM_W1 * TM_D * 2
     img_pg = align(p_out_16 + TM_D * TM_D * 2, 1024)
-    img_po = img_pg + 4 * TM_D * TM_D * 2
+    img_po = img_pg + 5 * TM_D * TM_D * 2  # p_a | g_a | p_b | g_b | g_out image
     return align(img_po + TM_D * TM_D * 2)
 
 
 def trimul_workspace_bytes(B: int, N: int, dtype: int) -> int:
-    """Tri-mult workspace: xn [P][128], h (fp32: [P][640]; 16-bit: g_out [P][128]), a|b channel-major
-    (or p_out's fp32 output, whichever is larger), o fp32 [B][128][N][N], 32 MiB cuBLAS scratch."""
-    P = B * N * N
-    es = 4 if dtype == F32 else 2
-    o = align(P * TM_D * es)
-    o = align(o + P * (TM_W1 if dtype == F32 else TM_D) * es)
-    o = align(o + max(2 * P * TM_D * es, P * TM_D * 4))
-    o = align(o + P * TM_D * 4)
-    return align(o + TRIMUL_BLAS_BYTES)
+    """Tri-mult workspace.  Channel planes of a, b and o are N rows of Np elements (16-bit: Np = N rounded
+    up to 8, 16-byte aligned rows for the contraction's TMA loads; fp32: Np = N).
+    fp32: xn [P][128], h [P][640], a|b (or p_out's fp32 output, whichever is larger), o, 32 MiB cuBLAS
+    scratch.  16-bit: g_out [P][128], a|b [2][B][128][N][Np], o fp32 [B][128][N][Np]."""
+    f32 = dtype == F32
+    Np = N if f32 else (N + 7) // 8 * 8
+    P, Pp = B * N * N, B * N * Np
+    es = 4 if f32 else 2
+    o = align(P * TM_D * es if f32 else 0)
+    o = align(o + P * (TM_W1 if f32 else TM_D) * es)
+    o = align(o + max(2 * Pp * TM_D * es, P * TM_D * 4 if f32 else 0))
+    o = align(o + Pp * TM_D * 4)
+    return align(o + (TRIMUL_BLAS_BYTES if f32 else 0))
