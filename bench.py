@@ -589,9 +589,9 @@ def run_trimul(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     cfg = CONFIGS[args.config]
-    N = cfg["N"]
+    N = args.case or cfg["N"]  # --case N: the same pair at a smaller N (ncu captures of a small case)
     prec = args.precision or cfg["dtype"]
-    z_h, pm_h, _, _ = make_config_inputs(args.config)
+    z_h, pm_h, _, _ = make_config_inputs(args.config, N=N)
     mods = [load_trimul_params(cls(128, precision=prec).to(dev), tm_params(cfg["seed_w"] + 50 + i))
             for i, cls in enumerate((TriangleMultiplicationOutgoing, TriangleMultiplicationIncoming))]
     z, mask = z_h.to(dev), pm_h.to(dev)
@@ -694,11 +694,14 @@ def main():
                     help="profiling case: run one start+end pair at this N once (after one warm-up pair), "
                          "check the device status and exit; nothing is timed")
     args = ap.parse_args()
+    if args.config is None:
+        args.config = 2  # one workload for every GPU count, so the driver's scaling ratios compare like with like
+    if args.layer == "trimul":
+        run_trimul(args)
+        return
     if args.case is not None:
         run_case(args)
         return
-    if args.config is None:
-        args.config = 2  # one workload for every GPU count, so the driver's scaling ratios compare like with like
     if args.layer == "trimul":
         run_trimul(args)
     elif args.impl == "b200" and "blocks" in CONFIGS[args.config]:

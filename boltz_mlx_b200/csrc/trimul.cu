@@ -381,42 +381,57 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
 //   incoming  A[i][k] = a[pl][k][i], B[j][k] = b[pl][k][j]  (MN-major operands: i / j contiguous)
 // a, b: [planes][N][Np] 16-bit, read by TMA through 3-D tensor maps (x = column, y = row, z = plane;
 // 128-byte swizzle; zero fill past N, so ragged edges and the K tail need no padding in memory).
-// o: fp32 [planes][N][Np].  Persistent, one CTA per SM, 192 threads: warp 0 lane 0 issues the TMA
-// loads, warp 1 lane 0 the MMAs, warps 2..5 are the epilogue (TMEM lane quadrant = warp % 4).  Tile =
-// 128 x 256 outputs of one plane (UMMA M = 128, N = 256, fp32 accumulation), K in blocks of 64 through
-// a ring of 4 stages of 48 KB; two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
-// overlap the main loop of the next.  Tiles are numbered plane-major (then row block, then column
-// block), so the CTAs running at the same time share a plane's a and b in L2.
-constexpr int CT_BM = 128, CT_BN = 256, CT_BK = 64, CT_STAGES = 4;
-constexpr int CT_A_BYTES = CT_BM * CT_BK * 2;  // 16 KB
-constexpr int CT_B_BYTES = CT_BN * CT_BK * 2;  // 32 KB
-constexpr int CT_STAGE = CT_A_BYTES + CT_B_BYTES;
-constexpr int CT_THREADS = 192;
-constexpr int CT_SMEM = 1024 + CT_STAGES * CT_STAGE + 256;  // + alignment slack + barriers
-static_assert(CT_SMEM <= 232448, "contraction shared memory");
+// o: fp32 [planes][N][Np].  Persistent, one CTA per SM: warp 0 lane 0 issues the TMA loads, warp 1
+// lane 0 the MMAs (UMMA M = 128, N = 256, fp32 accumulation in TMEM), the other warps are the epilogue
+// (one thread per output row; TMEM lane quadrant = warp % 4).  K runs in blocks of 64 through a ring of
+// shared-memory stages.  Two tile shapes:
+//   BM = 128: tile 128 x 256, 4 stages of 48 KB, two accumulators (2 x 256 TMEM columns) so that the
+//             epilogue of one tile overlaps the main loop of the next;
+//   BM = 256: tile 256 x 256 (two M = 128 MMAs share each B block: 2/3 of the operand bytes per flop),
+//             3 stages of 64 KB, one accumulator of 512 columns; the producer prefetches the next tile's
+//             first stages while the 8 epilogue warps drain it.
+// Tiles are numbered plane-major (then row block, then column block), so the CTAs running at the same
+// time share a plane's a and b in L2.
+template <int BM>
+struct CtCfg {
+  static constexpr int BN = 256, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BM == 128 ? 4 : 3;
+  static constexpr int ACCS = BM == 128 ? 2 : 1;  // accumulators of BM / 128 x 256 TMEM columns
+  static constexpr int EPI_WARPS = BM / 32;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + 256;  // + alignment slack + barriers
+  static_assert(SMEM <= 232448, "contraction shared memory");
+  static_assert(ACCS * (BM / 128) * 256 == 512, "TMEM columns");
+};
+#ifndef TRIATTN_CT_BM
+#define TRIATTN_CT_BM 128
+#endif
+constexpr int CT_BM = TRIATTN_CT_BM;  // tile shape used by the layer
 
-template <typename T, bool MN>
-__global__ void __launch_bounds__(CT_THREADS, 1)
+template <typename T, bool MN, int BM>
+__global__ void __launch_bounds__(CtCfg<BM>::THREADS, 1)
     tm_contract_tc_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                           float* __restrict__ o, int N, int Np, int planes, int* status) {
+  using C = CtCfg<BM>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-aligned stages
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + CT_STAGES * CT_STAGE);  // [STAGES] loads landed
-  uint64_t* empty = full + CT_STAGES;                                          // [STAGES] MMAs done reading
-  uint64_t* acc_full = empty + CT_STAGES;                                      // [2] accumulator complete
-  uint64_t* acc_empty = acc_full + 2;                                          // [2] accumulator read out
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);  // [STAGES] loads landed
+  uint64_t* empty = full + C::STAGES;                                          // [STAGES] MMAs done reading
+  uint64_t* acc_full = empty + C::STAGES;                                      // [ACCS] accumulator complete
+  uint64_t* acc_empty = acc_full + C::ACCS;                                    // [ACCS] accumulator read out
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + C::ACCS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mtn = (N + CT_BM - 1) / CT_BM, ntn = (N + CT_BN - 1) / CT_BN, nk = (N + CT_BK - 1) / CT_BK;
+  const int mtn = (N + BM - 1) / BM, ntn = (N + C::BN - 1) / C::BN, nk = (N + C::BK - 1) / C::BK;
   const int ntiles = planes * mtn * ntn;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < CT_STAGES; ++i) {
+    for (int i = 0; i < C::STAGES; ++i) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::ACCS; ++i) {
       mbar_init(acc_full + i, 1);
-      mbar_init(acc_empty + i, 4);
+      mbar_init(acc_empty + i, C::EPI_WARPS);
     }
     fence_mbar_init();
   }
@@ -427,9 +442,9 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
   const uint32_t tbase = *tslot;
   auto coords = [&](int t, int& pl, int& m0, int& n0) {
     const int r = t / ntn;
-    n0 = (t - r * ntn) * CT_BN;
+    n0 = (t - r * ntn) * C::BN;
     pl = r / mtn;
-    m0 = (r - pl * mtn) * CT_BM;
+    m0 = (r - pl * mtn) * BM;
   };
   if (warp == 0) {
     if (lane == 0) {
@@ -439,49 +454,52 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
         int pl, m0, n0;
         coords(t, pl, m0, n0);
         for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int st = it % CT_STAGES;
-          mbar_wait(empty + st, ((it / CT_STAGES) & 1) ^ 1, status, DEV_TIMEOUT_MMA);
-          unsigned char* sa = smem + st * CT_STAGE;
-          unsigned char* sb = sa + CT_A_BYTES;
-          mbar_arrive_expect_tx(full + st, CT_STAGE);
-          const int k0 = kb * CT_BK;
+          const int st = it % C::STAGES;
+          mbar_wait(empty + st, ((it / C::STAGES) & 1) ^ 1, status, DEV_TIMEOUT_MMA);
+          unsigned char* sa = smem + st * C::STAGE;
+          unsigned char* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(full + st, C::STAGE);
+          const int k0 = kb * C::BK;
           if constexpr (!MN) {
-            tma_load_3d(sa, &tma, k0, m0, pl, full + st);  // 128 rows x 64 k
+            tma_load_3d(sa, &tma, k0, m0, pl, full + st);  // BM rows x 64 k
             tma_load_3d(sb, &tmb, k0, n0, pl, full + st);  // 256 rows x 64 k
           } else {
 #pragma unroll
-            for (int q = 0; q < CT_BM / 64; ++q) tma_load_3d(sa + q * 8192, &tma, m0 + 64 * q, k0, pl, full + st);
+            for (int q = 0; q < BM / 64; ++q) tma_load_3d(sa + q * 8192, &tma, m0 + 64 * q, k0, pl, full + st);
 #pragma unroll
-            for (int q = 0; q < CT_BN / 64; ++q) tma_load_3d(sb + q * 8192, &tmb, n0 + 64 * q, k0, pl, full + st);
+            for (int q = 0; q < C::BN / 64; ++q) tma_load_3d(sb + q * 8192, &tmb, n0 + 64 * q, k0, pl, full + st);
           }
         }
       }
       // copies still in flight after an error: wait (bounded) for the last load of every stage
-      for (int st = 0; st < CT_STAGES && st < it; ++st) {
-        const int last = it - 1 - ((it - 1 - st) % CT_STAGES);
-        mbar_wait_drain(full + st, (last / CT_STAGES) & 1, 200000000ull);
+      for (int st = 0; st < C::STAGES && st < it; ++st) {
+        const int last = it - 1 - ((it - 1 - st) % C::STAGES);
+        mbar_wait_drain(full + st, (last / C::STAGES) & 1, 200000000ull);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---- MMA issuer ----
-      constexpr uint32_t idesc = make_idesc_f16(CT_BM, CT_BN, H16<T>::is_bf16, MN ? 1 : 0, MN ? 1 : 0);
+      // ---- MMA issuer: per K step of 16, BM / 128 MMAs of 128 x 256 sharing the B block ----
+      constexpr uint32_t idesc = make_idesc_f16(128, C::BN, H16<T>::is_bf16, MN ? 1 : 0, MN ? 1 : 0);
       int it = 0, tl = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
-        const int acc = tl & 1;
-        mbar_wait(acc_empty + acc, ((tl >> 1) & 1) ^ 1, status, DEV_TIMEOUT_MMA);
+        const int acc = tl % C::ACCS;
+        mbar_wait(acc_empty + acc, ((tl / C::ACCS) & 1) ^ 1, status, DEV_TIMEOUT_MMA);
         tc_fence_after();
-        const uint32_t d = tbase + acc * CT_BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int st = it % CT_STAGES;
-          mbar_wait(full + st, (it / CT_STAGES) & 1, status, DEV_TIMEOUT_TMA);
+          const int st = it % C::STAGES;
+          mbar_wait(full + st, (it / C::STAGES) & 1, status, DEV_TIMEOUT_TMA);
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + st * CT_STAGE), sb = sa + CT_A_BYTES;
+          const uint32_t sa = smem_u32(smem + st * C::STAGE), sb = sa + C::A_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < CT_BK / 16; ++ks) {
-            const uint64_t ad = MN ? smem_desc_sw128_mn(sa + ks * 2048, 8192) : smem_desc_sw128(sa + ks * 32);
+          for (int ks = 0; ks < C::BK / 16; ++ks) {
             const uint64_t bd = MN ? smem_desc_sw128_mn(sb + ks * 2048, 8192) : smem_desc_sw128(sb + ks * 32);
-            umma_ss(d, ad, bd, idesc, (kb | ks) ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < BM / 128; ++h) {
+              const uint32_t sah = sa + h * 16384;  // rows 128 h.. of the A block (either layout)
+              const uint64_t ad = MN ? smem_desc_sw128_mn(sah + ks * 2048, 8192) : smem_desc_sw128(sah + ks * 32);
+              umma_ss(tbase + (acc + h) * 256, ad, bd, idesc, (kb | ks) ? 1u : 0u);
+            }
           }
           umma_commit(empty + st);  // the stage is free once these MMAs have read it
         }
@@ -489,31 +507,31 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       }
     }
   } else {
-    // ---- epilogue: rows m0 + 32 q + lane, fp32 stores of 32 columns at a time ----
-    const int q = warp & 3;
+    // ---- epilogue: one thread per output row, fp32 stores of 32 columns at a time ----
+    const int e = warp - 2, q = warp & 3, h = e >> 2;  // rows m0 + 128 h + 32 q + lane
     int tl = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
       int pl, m0, n0;
       coords(t, pl, m0, n0);
-      const int acc = tl & 1;
-      mbar_wait(acc_full + acc, (tl >> 1) & 1, status, DEV_TIMEOUT_MMA);
+      const int acc = tl % C::ACCS;
+      mbar_wait(acc_full + acc, (tl / C::ACCS) & 1, status, DEV_TIMEOUT_MMA);
       __syncwarp();
       tc_fence_after();
-      const int i = m0 + 32 * q + lane;
+      const int i = m0 + 128 * h + 32 * q + lane;
       float* orow = o + ((long long)pl * N + (i < N ? i : 0)) * Np;
 #pragma unroll 1
-      for (int c = 0; c < CT_BN / 32; ++c) {
+      for (int c = 0; c < C::BN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem_addr(tbase + acc * CT_BN, 32 * q, 32 * c), v);
+        tmem_ld32(tmem_addr(tbase + (acc + h) * 256, 32 * q, 32 * c), v);
         tmem_ld_wait();
         tmem_regs_ready(v);
         const int j0 = n0 + 32 * c;
         if (i < N) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            if (j0 + e < Np)
-              *reinterpret_cast<float4*>(orow + j0 + e) = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                                                                      __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+          for (int e4 = 0; e4 < 32; e4 += 4)
+            if (j0 + e4 < Np)
+              *reinterpret_cast<float4*>(orow + j0 + e4) = make_float4(
+                  __uint_as_float(v[e4]), __uint_as_float(v[e4 + 1]), __uint_as_float(v[e4 + 2]), __uint_as_float(v[e4 + 3]));
         }
       }
       tc_fence_before();
@@ -797,6 +815,30 @@ cudaError_t encode_planes(CUtensorMap* m, const void* base, bool bf16, int N, in
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// G2 launch: tensor maps of the a and b planes (outgoing: K-major boxes of 64 k x BM (a) / 256 (b) rows;
+// incoming: MN-major boxes of 64 columns x 64 k), one persistent CTA per SM.
+template <typename T, int BM>
+cudaError_t launch_contract(const T* ab, bool bf16, bool outgoing, float* o, int N, int Np, int planes, int sms,
+                            int* status, cudaStream_t st) {
+  using C = CtCfg<BM>;
+  CUtensorMap ma, mb;
+  cudaError_t e;
+  if ((e = encode_planes(&ma, ab, bf16, N, Np, planes, outgoing ? BM : C::BK)) != cudaSuccess) return e;
+  if ((e = encode_planes(&mb, ab + (size_t)planes * N * Np, bf16, N, Np, planes, outgoing ? C::BN : C::BK)) !=
+      cudaSuccess)
+    return e;
+  const int ctiles = planes * ((N + BM - 1) / BM) * ((N + C::BN - 1) / C::BN);
+  const int grid = ctiles < sms ? ctiles : sms;
+  if (outgoing) {
+    cudaFuncSetAttribute(tm_contract_tc_kernel<T, false, BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    tm_contract_tc_kernel<T, false, BM><<<grid, C::THREADS, C::SMEM, st>>>(ma, mb, o, N, Np, planes, status);
+  } else {
+    cudaFuncSetAttribute(tm_contract_tc_kernel<T, true, BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    tm_contract_tc_kernel<T, true, BM><<<grid, C::THREADS, C::SMEM, st>>>(ma, mb, o, N, Np, planes, status);
+  }
+  return cudaGetLastError();
+}
+
 // 16-bit modes: F1 projection -> G2 contraction -> T1 tail, all hand-written tcgen05 kernels.
 template <typename T>
 cudaError_t trimul_run16(const TrimulArgs& a, cudaStream_t st, const char** stage) {
@@ -820,23 +862,9 @@ cudaError_t trimul_run16(const TrimulArgs& a, cudaStream_t st, const char** stag
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   *stage = "contraction";
-  CUtensorMap ma, mb;
   const bool bf16 = a.dtype == DT_BF16;
-  // outgoing: K-major boxes of 64 k x 128 (a) / 256 (b) rows; incoming: MN-major boxes of 64 columns x 64 k
-  if ((e = encode_planes(&ma, ab, bf16, N, Np, planes, a.outgoing ? CT_BM : CT_BK)) != cudaSuccess) return e;
-  if ((e = encode_planes(&mb, ab + (size_t)planes * N * Np, bf16, N, Np, planes, a.outgoing ? CT_BN : CT_BK)) !=
-      cudaSuccess)
+  if ((e = launch_contract<T, CT_BM>(ab, bf16, a.outgoing != 0, o, N, Np, planes, sms, status, st)) != cudaSuccess)
     return e;
-  const int ctiles = planes * ((N + CT_BM - 1) / CT_BM) * ((N + CT_BN - 1) / CT_BN);
-  const int cgrid = ctiles < sms ? ctiles : sms;
-  if (a.outgoing) {
-    cudaFuncSetAttribute(tm_contract_tc_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
-    tm_contract_tc_kernel<T, false><<<cgrid, CT_THREADS, CT_SMEM, st>>>(ma, mb, o, N, Np, planes, status);
-  } else {
-    cudaFuncSetAttribute(tm_contract_tc_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
-    tm_contract_tc_kernel<T, true><<<cgrid, CT_THREADS, CT_SMEM, st>>>(ma, mb, o, N, Np, planes, status);
-  }
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   *stage = "tail";
   const int grid = (int)((P + TILE - 1) / TILE);
