@@ -463,6 +463,31 @@ def run_b200(args):
     e1.record(stream)
     torch.cuda.synchronize()
     core_ms = e0.elapsed_time(e1) / core_iters
+    # the two HBM-bound stages timed alone the same way (start-node views; out_proj writes t2, which the
+    # e2e section below overwrites)
+    def time_launch(fn, iters=10):
+        for _ in range(2):
+            fn()
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+    stage_ms = {
+        f"ln_proj_{nd}": time_launch(lambda st_=st_: _lib.check(L.triattn_ln_proj(
+            t1.data_ptr(), packs[1].data_ptr(), 1, N, st_, 0, N, dt, work.data_ptr(), wsb, sh)))
+        for nd, st_ in (("start", 1), ("end", 0))
+    }
+    stage_ms.update({
+        f"out_proj_{nd}": time_launch(lambda st_=st_: _lib.check(L.triattn_out_proj(
+            t1.data_ptr(), packs[1].data_ptr(), 1, N, st_, 0, N, dt, 1, t2.data_ptr(), work.data_ptr(), wsb, sh)))
+        for nd, st_ in (("start", 1), ("end", 0))
+    })
+    hbm = peaks()[0].get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    stage_bytes = {"ln_proj": 1544 * N * N, "out_proj": 1536 * N * N}  # algorithmic bytes per launch
+    stages = {k: {"ms": v, "frac_hbm": stage_bytes[k.rsplit("_", 1)[0]] / (v * 1e-3) / 1e9 / hbm}
+              for k, v in stage_ms.items()}
     pk, pk_kind = peaks()
     tensor_peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     achieved = fl["core"] / (core_ms * 1e-3) / 1e12
@@ -558,6 +583,8 @@ def run_b200(args):
                 "pipelined": "input copy, pair and output copy of consecutive steps overlap (2 device slots)"},
         "gpu_launches": args.steps * layers * 4,
         "clocks": clk.summary(),
+        "stages": {**stages, "note": "HBM-bound stages timed alone with CUDA events (10 launches); frac_hbm = "
+                   "algorithmic bytes (ln_proj 1544 B, out_proj 1536 B per pair) / time / measured copy peak"},
     }
     if nested is not None:
         line["config4_same_gpus"] = nested

@@ -40,17 +40,37 @@ __device__ __forceinline__ float ex2(float x) {
 // =================================================================================================
 // LN + q|k|v|g projection (+ tri bias).  Persistent: one CTA per SM (512 threads) loads the 128 KB
 // weight image once and walks the 128-pair tiles (a, c0..c0+127) tile = blockIdx.x, + gridDim.x, ...
-// Per tile: LayerNorm (warp w: pairs 8w..8w+7, lane: channels 4 lane..+3) -> operand image in shared
-// memory + tri-bias rows; the z rows of the next tile are loaded into registers right after the
-// LayerNorm, so their HBM latency overlaps the MMA and the epilogue.  MMA: D[128 x 512] = xn * W^T
-// in two N=256 halves (q|k, v|g) with separate commits, so the q|k epilogue starts while v|g runs.
-// Epilogue: warp w reads TMEM lanes 32 (w % 4).. and writes output type w / 4 (q, k, v, g).
+// Warp-specialised, so that the LayerNorm of one tile runs while the previous tile is written out:
+//   LN group (warps 0..7): LayerNorm of tile i -> operand image i & 1 in shared memory (128-byte
+//     swizzle) + tri-bias row sums; warp w holds pairs 16w..16w+15 in two passes of 8, four lanes per
+//     pair (lane & 3 = qq: channels 16 j + 4 qq .. + 3, j = 0..7: a pair's four lanes load 64 contiguous
+//     bytes at a time), so a statistic is a thread-local sum plus two shuffles and the four head sums of
+//     the tri bias end one per lane after four shuffles; the LayerNorm affine and tri-bias weights are read
+//     from shared memory.  The z rows of tile i + 1 are loaded into registers right after the LayerNorm of
+//     tile i.
+//     Warps 2 and 3 write the tile's tri-bias block once the group's row sums are complete.
+//   drain group (warps 8..15): warp (part, quadrant) reads TMEM lanes 32 quadrant.. of half `part` and
+//     writes q (x C^-1/2 log2 e) and k as K-major images, or v (MN-major image) and g (row-major, + gate
+//     bias).  Warp 8 lane 0 issues the MMA D[128 x 512] = xn W^T of tile i in two N = 256 halves (q|k into
+//     TMEM columns 0..255, v|g into 256..511) once image i is complete, each half as soon as that half of
+//     tile i - 1 has been drained; one commit per half.
 // TMEM: 512 columns = the full 128 x 512 fp32 accumulator of one tile.
 // =================================================================================================
-constexpr int LP_THREADS = 512;
+#ifndef TRIATTN_LP_LN_WARPS
+#define TRIATTN_LP_LN_WARPS 8
+#endif
+constexpr int LP_LN_WARPS = TRIATTN_LP_LN_WARPS;                 // LayerNorm group: 8 or 16 pairs per warp
+constexpr int LP_DRAIN_WARPS = LP_LN_WARPS == 8 ? 8 : 4;        // drain group: 4 warps per TMEM half, or 4 for both
+constexpr int LP_PARTS = LP_DRAIN_WARPS / 4;                    // TMEM halves per drain warp: 2 -> 1 each, 1 -> both
+constexpr int LP_THREADS = 32 * (LP_LN_WARPS + LP_DRAIN_WARPS);
 constexpr int LP_W_BYTES = NPROJ * C_IN * 2;  // 131072
 constexpr int LP_A_BYTES = TILE * C_IN * 2;   // 32768
-constexpr int LP_SMEM = LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4 + 64;
+constexpr int LP_SW = LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4;  // ln_w, ln_b, w_b [4] (fp32)
+constexpr int LP_SMEM = LP_SW + (2 + HEADS) * C_IN * 4 + 128;
+#ifndef TRIATTN_LP_PREFETCH
+#define TRIATTN_LP_PREFETCH 2
+#endif
+constexpr int LP_PREFETCH = TRIATTN_LP_PREFETCH;  // tiles whose rows are in L2 ahead of the register loads
 
 template <typename T, bool XN, bool TB>
 __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs args) {
@@ -59,10 +79,14 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   unsigned char* sA = smem + LP_W_BYTES;
   float* sBias = reinterpret_cast<float*>(smem + LP_W_BYTES + 2 * LP_A_BYTES);  // [2][4][128]
   float* sGb = reinterpret_cast<float*>(smem + LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4);  // g bias [128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_W_BYTES + 2 * LP_A_BYTES + 2 * HEADS * TILE * 4 + C_IN * 4);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
-  uint64_t* bar_w = bars;
-  uint64_t* bar_mma = bars + 1;  // [2]: q|k half, v|g half
+  float* sLw = reinterpret_cast<float*>(smem + LP_SW);  // [2 + HEADS][128]: ln_w, ln_b, w_b rows
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LP_SW + (2 + HEADS) * C_IN * 4);
+  uint64_t* bar_w = bars;         // weight image landed
+  uint64_t* bar_mma = bars + 1;   // [2] MMA half (q|k, v|g) of the current tile complete
+  uint64_t* bar_tmem = bars + 3;  // [2] that half drained (4 warps each)
+  uint64_t* bar_img = bars + 5;   // [2] every MMA reading operand image s complete
+  uint64_t* bar_ready = bars + 7;  // [2] the LN group's operand image s is complete (one completion per use)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 9);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int N = args.N, R = args.row_end - args.row_begin, NT = args.wl.NT;
@@ -77,11 +101,18 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
   }
   if (tid == 0) {
     mbar_init(bar_w, 1);
-    mbar_init(bar_mma + 0, 1);
-    mbar_init(bar_mma + 1, 1);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(bar_mma + h, 1);
+      mbar_init(bar_tmem + h, 4);
+      mbar_init(bar_img + h, 1);
+      mbar_init(bar_ready + h, 1);
+    }
     fence_mbar_init();
   }
   if (tid < C_IN) sGb[tid] = P[PackedLayout::g_b / 4 + tid];
+  for (int i = tid; i < (2 + HEADS) * C_IN; i += LP_THREADS)
+    sLw[i] = i < C_IN ? P[PackedLayout::ln_w / 4 + i]
+                      : (i < 2 * C_IN ? P[PackedLayout::ln_b / 4 + i - C_IN] : P[PackedLayout::w_b / 4 + i - 2 * C_IN]);
   if (warp == 0) tmem_alloc(tslot, 512);
   tc_fence_before();
   __syncthreads();
@@ -91,212 +122,279 @@ __global__ void __launch_bounds__(LP_THREADS, 1) ln_proj_tc_kernel(LayerArgs arg
     mbar_arrive_expect_tx(bar_w, LP_W_BYTES);
     bulk_g2s(sW, args.packed + PackedLayout::img_qkvg, LP_W_BYTES, bar_w);
   }
-
-  const float4 lw = reinterpret_cast<const float4*>(P + PackedLayout::ln_w / 4)[lane];
-  const float4 lb = reinterpret_cast<const float4*>(P + PackedLayout::ln_b / 4)[lane];
-  float4 wb[HEADS];
-#pragma unroll
-  for (int hh = 0; hh < HEADS; ++hh) wb[hh] = reinterpret_cast<const float4*>(P + PackedLayout::w_b / 4 + hh * C_IN)[lane];
-  // this warp's 8 z rows of a tile (zeros past N)
   // caller-given LayerNorm output (16-bit, this layer's type): the LN is skipped and its bits become
   // the operand image as they are (kernel-uniform)
   constexpr bool xn_mode = XN;
   // the producer of xn also gave this layer's tri bias (args.tb_in): the SIMT tri-bias dot is skipped
   constexpr bool tb_given = XN && TB;
-  auto load_rows = [&](int tile, float4 (&xv)[8]) {
-    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
-    if constexpr (xn_mode) {
-      // lane: 4 channels = 8 bytes, kept in .x/.y
-      const uint16_t* xr = reinterpret_cast<const uint16_t*>(args.xn) + b * args.xnv.s_batch +
-                           (long long)(args.row_begin + al - args.xnv.row0) * args.xnv.s_row;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int c = ct * TILE + warp * 8 + i;
-        const uint2 u = c < N ? __ldcs(reinterpret_cast<const uint2*>(xr + view_col(args.xnv, c)) + lane)
-                              : make_uint2(0u, 0u);
-        xv[i] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), 0.f, 0.f);
+
+    // the z (or xn) rows of a tile pulled into L2 ahead of their register loads: rows that are contiguous
+    // in memory (a dense view whose columns are consecutive pairs) as one bulk prefetch, otherwise one
+    // bulk prefetch per row (512 B of fp32 z, 256 B of 16-bit xn) spread over the drain group's threads (the bulk-copy unit takes them one at a time, off the
+    // LayerNorm group's path)
+    const View& pv = xn_mode ? args.xnv : args.zv;
+    const bool rows_contiguous = !pv.cblk && pv.s_col == C_IN;
+    constexpr int ROW_BYTES = xn_mode ? C_IN * 2 : C_IN * 4;
+    auto prefetch_rows = [&](int tile, int e) {  // e: this thread's index in the issuing group
+      if (tile >= ntiles) return;
+      const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+      const unsigned char* base =
+          (xn_mode ? static_cast<const unsigned char*>(args.xn) : reinterpret_cast<const unsigned char*>(args.z)) +
+          (b * pv.s_batch + (long long)(args.row_begin + al - pv.row0) * pv.s_row) * (ROW_BYTES / C_IN);
+      const int c0 = ct * TILE, rows = min(TILE, N - c0);
+      if (rows_contiguous) {
+        if (e == 0) prefetch_l2_bulk(base + (long long)c0 * ROW_BYTES, rows * ROW_BYTES);
+      } else if (e < rows) {
+        prefetch_l2_bulk(base + view_col(pv, c0 + e) * (ROW_BYTES / C_IN), ROW_BYTES);
       }
-      return;
-    }
-    const float* zr = args.z + b * args.zv.s_batch + (long long)(args.row_begin + al - args.zv.row0) * args.zv.s_row;
+    };
+  if (warp < LP_LN_WARPS) {
+    // ================================ LN group ================================
+    const int qq = lane & 3;
+    constexpr int PASSES = 128 / (8 * LP_LN_WARPS);  // groups of 8 pairs per warp
+    // rows (PASSES warp + pass) 8 + lane / 4 of a tile: xv[pass][j] = channels 16 j + 4 qq .. + 3 (zeros
+    // past N; xn mode: 4 16-bit values in .x / .y)
+    auto load_rows = [&](int tile, int ps, float4 (&xvp)[8]) {
+      const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+      {
+        const int c = ct * TILE + 8 * (PASSES * warp + ps) + (lane >> 2);
+        if constexpr (xn_mode) {
+          const uint16_t* xr = reinterpret_cast<const uint16_t*>(args.xn) + b * args.xnv.s_batch +
+                               (long long)(args.row_begin + al - args.xnv.row0) * args.xnv.s_row;
+          const uint2* src = reinterpret_cast<const uint2*>(xr + (c < N ? view_col(args.xnv, c) : 0)) + qq;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int c = ct * TILE + warp * 8 + i;
-      xv[i] = c < N ? __ldcs(reinterpret_cast<const float4*>(zr + view_col(args.zv, c)) + lane)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  // ---- one tile in three steps: LayerNorm into image it & 1, MMA, epilogue.  The LayerNorm of tile
-  //      it + 1 runs while the MMA of tile it executes (two operand images, two tri-bias buffers);
-  //      one CTA barrier per tile then hands over both the new image and the freed TMEM ----
-  auto ln_tile = [&](int it, const float4 (&xv)[8]) {
-    float* sB = sBias + (it & 1) * HEADS * TILE;
-    unsigned char* sAi = sA + (it & 1) * LP_A_BYTES;
-    // ---- LayerNorm of this warp's 8 rows -> operand image + tri-bias values ----
+          for (int j = 0; j < 8; ++j) {
+            const uint2 u = c < N ? __ldcs(src + 4 * j) : make_uint2(0u, 0u);
+            xvp[j] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), 0.f, 0.f);
+          }
+        } else {
+          const float* zr =
+              args.z + b * args.zv.s_batch + (long long)(args.row_begin + al - args.zv.row0) * args.zv.s_row;
+          const float4* src = reinterpret_cast<const float4*>(zr + (c < N ? view_col(args.zv, c) : 0)) + qq;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = warp * 8 + i;
-      const float4 v = xv[i];
-      float n0, n1, n2, n3;
-      uint2 pk;
-      if constexpr (xn_mode) {
-        pk = make_uint2(__float_as_uint(v.x), __float_as_uint(v.y));
-        const float2 a01 = H16<T>::unpack(pk.x), a23 = H16<T>::unpack(pk.y);
-        n0 = a01.x; n1 = a01.y; n2 = a23.x; n3 = a23.y;
-      } else {
-        const float mean = warp_sum32(v.x + v.y + v.z + v.w) * (1.0f / C_IN);
-        const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
-        const float var = warp_sum32(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / C_IN);
-        const float rstd = rsqrtf(var + LN_EPS);
-        n0 = d0 * rstd * lw.x + lb.x; n1 = d1 * rstd * lw.y + lb.y;
-        n2 = d2 * rstd * lw.z + lb.z; n3 = d3 * rstd * lw.w + lb.w;
-        pk.x = H16<T>::pack(n0, n1);
-        pk.y = H16<T>::pack(n2, n3);
+          for (int j = 0; j < 8; ++j) xvp[j] = c < N ? __ldcs(src + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
-      // swizzled image: one row's 256 bytes are two 128-byte runs (no bank conflicts)
-      *reinterpret_cast<uint2*>(sAi + sw128_off(r, 4 * lane, LP_A_BYTES / 2)) = pk;
-      // the four head sums of this row's tri bias at once; lane 8 hh ends with head hh's total
+    };
+    auto ln_rows = [&](int it, int ps, const float4 (&xv)[8]) {
+      float* sB = sBias + (it & 1) * HEADS * TILE;
+      unsigned char* sAi = sA + (it & 1) * LP_A_BYTES;
+      const int rw = 8 * (PASSES * warp + ps) + (lane >> 2);
+      const float4* w4 = reinterpret_cast<const float4*>(sLw) + qq;  // row q of sLw: w4[32 q + 4 j]
+      // packed fp32 pairs (f32x2 instructions): a = channels (16 j + 4 qq, + 1), b = (+ 2, + 3)
+      auto lo = [](const float4& v) { return make_float2(v.x, v.y); };
+      auto hi = [](const float4& v) { return make_float2(v.z, v.w); };
+      float2 nmean = make_float2(0.f, 0.f), rstd2 = make_float2(0.f, 0.f);
+      if constexpr (!xn_mode) {
+        float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s2 = __fadd2_rn(s2, __fadd2_rn(lo(xv[j]), hi(xv[j])));
+        float s = s2.x + s2.y;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        const float mean = s * (1.0f / C_IN);
+        nmean = make_float2(-mean, -mean);
+        float2 v2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float2 da = __fadd2_rn(lo(xv[j]), nmean), db = __fadd2_rn(hi(xv[j]), nmean);
+          v2 = __ffma2_rn(da, da, v2);
+          v2 = __ffma2_rn(db, db, v2);
+        }
+        float v = v2.x + v2.y;
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        const float rstd = rsqrtf(v * (1.0f / C_IN) + LN_EPS);
+        rstd2 = make_float2(rstd, rstd);
+      }
+      // head sums as pairs (even, odd channel), added up at the end
+      float2 p2[HEADS] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float2 na, nb;
+        uint2 pk;
+        if constexpr (xn_mode) {
+          pk = make_uint2(__float_as_uint(xv[j].x), __float_as_uint(xv[j].y));
+          na = H16<T>::unpack(pk.x);
+          nb = H16<T>::unpack(pk.y);
+        } else {
+          const float4 lw = w4[4 * j], lb = w4[32 + 4 * j];
+          na = __ffma2_rn(__fmul2_rn(__fadd2_rn(lo(xv[j]), nmean), rstd2), lo(lw), lo(lb));
+          nb = __ffma2_rn(__fmul2_rn(__fadd2_rn(hi(xv[j]), nmean), rstd2), hi(lw), hi(lb));
+          pk.x = H16<T>::pack(na.x, na.y);
+          pk.y = H16<T>::pack(nb.x, nb.y);
+        }
+        // swizzled image: the 8 bytes of channels 16 j + 4 qq .. + 3 of row rw
+        *reinterpret_cast<uint2*>(sAi + sw128_off(rw, 16 * j + 4 * qq, LP_A_BYTES / 2)) = pk;
+        if constexpr (!tb_given) {
+#pragma unroll
+          for (int hh = 0; hh < HEADS; ++hh) {
+            const float4 wb = w4[32 * (2 + hh) + 4 * j];
+            p2[hh] = __ffma2_rn(na, lo(wb), p2[hh]);
+            p2[hh] = __ffma2_rn(nb, hi(wb), p2[hh]);
+          }
+        }
+      }
+      float p[HEADS];
+#pragma unroll
+      for (int hh = 0; hh < HEADS; ++hh) p[hh] = p2[hh].x + p2[hh].y;
       if constexpr (!tb_given) {
-        float p[HEADS];
-#pragma unroll
-        for (int hh = 0; hh < HEADS; ++hh) p[hh] = n0 * wb[hh].x + n1 * wb[hh].y + n2 * wb[hh].z + n3 * wb[hh].w;
-        const float k = head_sums4(p, lane);
-        if ((lane & 7) == 0) sB[(lane >> 3) * TILE + r] = k;
+        // the row's four head sums over its four lanes: exchange halves (xor 2: heads 0,1 | 2,3), then one
+        // head each (xor 1); lane qq ends with head qq's total
+        const bool up2 = qq & 2, up1 = qq & 1;
+        float k0 = up2 ? p[2] : p[0], k1 = up2 ? p[3] : p[1];
+        k0 += __shfl_xor_sync(0xffffffffu, up2 ? p[0] : p[2], 2);
+        k1 += __shfl_xor_sync(0xffffffffu, up2 ? p[1] : p[3], 2);
+        float k = up1 ? k1 : k0;
+        k += __shfl_xor_sync(0xffffffffu, up1 ? k0 : k1, 1);
+        sB[qq * TILE + rw] = k;
       }
-    }
-  };
-  auto issue_mma = [&](int it) {
-    unsigned char* sAi = sA + (it & 1) * LP_A_BYTES;
-    // ---- MMA: two N=256 halves, one commit each ----
-    if (tid == 0) {
-      if (it == 0) mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
-      tc_fence_after();
-      constexpr uint32_t idesc = make_idesc_f16(128, 256, H16<T>::is_bf16, 0, 0);
+    };
+    float4 xv[PASSES][8];
+    int tile = blockIdx.x;
+    if (tile < ntiles)
 #pragma unroll
-      for (int nh = 0; nh < 2; ++nh) {
+      for (int ps = 0; ps < PASSES; ++ps) load_rows(tile, ps, xv[ps]);
+    for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
+      // operand image it & 1 is free once every MMA of tile it - 2 has completed (tri-bias slot it & 1 was
+      // last read by warps 2, 3 before the group barrier of tile it - 1)
+      if (it >= 2) mbar_wait(bar_img + (it & 1), ((it >> 1) - 1) & 1, status, DEV_TIMEOUT_MMA);
+      // each pass's registers take the next tile's rows as soon as the pass is done (in flight for a tile)
 #pragma unroll
-        for (int ks = 0; ks < C_IN / 16; ++ks) {
-          const uint64_t ad = smem_desc_sw128(smem_u32(sAi) + (ks / 4) * (LP_A_BYTES / 2) + (ks % 4) * 32);
-          const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * C_IN);
-          umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
-        }
-        umma_commit(bar_mma + nh);
+      for (int ps = 0; ps < PASSES; ++ps) {
+        ln_rows(it, ps, xv[ps]);
+        if (tile + (int)gridDim.x < ntiles) load_rows(tile + gridDim.x, ps, xv[ps]);
       }
-    }
-
-  };
-  auto tri_bias = [&](int it, int tile) {
-    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
-    const int a = args.row_begin + al, c0 = ct * TILE;
-    const float* sB = sBias + (it & 1) * HEADS * TILE;
-    // ---- tri-bias rows of attention row a: fp16, log2 domain, 128 x 128 block layout [k/8][q][8];
-    //      one 16-byte chunk = 8 consecutive keys of one head (padded keys 0) ----
-    //      (a producer-given tri bias: fp16 [B][HEADS][N][N], element (b, hh, a, c))
-    if (tid < HEADS * (TILE / 8)) {
-      const int hh = tid / (TILE / 8), kg = tid % (TILE / 8);
-      const __half* tbr = tb_given ? static_cast<const __half*>(args.tb_in) + (((size_t)b * HEADS + hh) * N + a) * N : nullptr;
-      auto bias_at = [&](int r0) -> float {
-        if (c0 + r0 >= N) return 0.0f;
-        return (tb_given ? __half2float(tbr[c0 + r0]) : sB[hh * TILE + r0]) * LOG2E;
-      };
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r0 = kg * 8 + 2 * i;
-        w[i] = H16<__half>::pack(bias_at(r0), bias_at(r0 + 1));
-      }
-      *reinterpret_cast<uint4*>(args.ws + args.wl.off_bias + bias16_off(a, c0 + kg * 8, b, hh, args.B, NT)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
-    }
-
-  };
-  auto epilogue = [&](int it, int tile) {
-    const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
-    const int c0 = ct * TILE;
-    // ---- epilogue: warp w reads lanes 32*(w%4).., output type w/4 (0 q, 1 k, 2 v, 3 g) ----
-    const int quad = warp & 3, tt = warp >> 2;
-    const int r = quad * 32 + lane, c = c0 + r;
-    const bool valid = c < N;
-    mbar_wait(bar_mma + (tt >> 1), it & 1, status, DEV_TIMEOUT_MMA);
-    __syncwarp();
-    tc_fence_after();
-#pragma unroll 1
-    for (int hh = 0; hh < HEADS; ++hh) {
-      uint32_t acc[32];
-      tmem_ld32(tmem_addr(tbase, quad * 32, tt * 128 + hh * 32), acc);
-      tmem_ld_wait();
-      tmem_regs_ready(acc);
-      if (tt == 0 || tt == 1) {
-        // q (pre-scaled by C^-1/2 log2 e: the core's S is then in log2 units) and k: K-major images
-        const float sc = tt == 0 ? QSCALE_L2 : 1.0f;
-        unsigned char* img = args.ws + (tt == 0 ? args.wl.off_q : args.wl.off_k) +
-                             ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
-#pragma unroll
-        for (int d = 0; d < C_HEAD; d += 8) {
-          uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-          if (valid) {
-            pk.x = H16<T>::pack(__uint_as_float(acc[d + 0]) * sc, __uint_as_float(acc[d + 1]) * sc);
-            pk.y = H16<T>::pack(__uint_as_float(acc[d + 2]) * sc, __uint_as_float(acc[d + 3]) * sc);
-            pk.z = H16<T>::pack(__uint_as_float(acc[d + 4]) * sc, __uint_as_float(acc[d + 5]) * sc);
-            pk.w = H16<T>::pack(__uint_as_float(acc[d + 6]) * sc, __uint_as_float(acc[d + 7]) * sc);
-          }
-          *reinterpret_cast<uint4*>(img + img_off(r, d, C_HEAD)) = pk;
-        }
-      } else if (tt == 2) {
-        // v: fp16 in every 16-bit mode (the P.V product runs in fp16), saturated to the fp16 range,
-        // MN-major image read by the P.V MMA
-        unsigned char* img = args.ws + args.wl.off_v + ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
-        auto sat = [](uint32_t u) { return fminf(fmaxf(__uint_as_float(u), -65504.f), 65504.f); };
-#pragma unroll
-        for (int d = 0; d < C_HEAD; d += 8) {
-          uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-          if (valid) {
-            pk.x = H16<__half>::pack(sat(acc[d + 0]), sat(acc[d + 1]));
-            pk.y = H16<__half>::pack(sat(acc[d + 2]), sat(acc[d + 3]));
-            pk.z = H16<__half>::pack(sat(acc[d + 4]), sat(acc[d + 5]));
-            pk.w = H16<__half>::pack(sat(acc[d + 6]), sat(acc[d + 7]));
-          }
-          *reinterpret_cast<uint4*>(img + vimg_off(r, d)) = pk;
-        }
-      } else if (valid) {
-        const float* gb = sGb + hh * C_HEAD;
-        T* g = reinterpret_cast<T*>(args.ws + args.wl.off_g) + (((size_t)b * R + al) * N + c) * C_IN + hh * C_HEAD;
-#pragma unroll
-        for (int d = 0; d < C_HEAD; d += 8) {
-          uint4 pk;
-          pk.x = H16<T>::pack(__uint_as_float(acc[d + 0]) + gb[d + 0], __uint_as_float(acc[d + 1]) + gb[d + 1]);
-          pk.y = H16<T>::pack(__uint_as_float(acc[d + 2]) + gb[d + 2], __uint_as_float(acc[d + 3]) + gb[d + 3]);
-          pk.z = H16<T>::pack(__uint_as_float(acc[d + 4]) + gb[d + 4], __uint_as_float(acc[d + 5]) + gb[d + 5]);
-          pk.w = H16<T>::pack(__uint_as_float(acc[d + 6]) + gb[d + 6], __uint_as_float(acc[d + 7]) + gb[d + 7]);
-          *reinterpret_cast<uint4*>(g + d) = pk;
-        }
-      }
-    }
-  };
-  float4 xv[8];
-  int tile = blockIdx.x;
-  if (tile < ntiles) {
-    load_rows(tile, xv);
-    ln_tile(0, xv);
-    if (tile + (int)gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
-    fence_proxy_async_smem();
-    __syncthreads();
-    issue_mma(0);
-  }
-  for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
-    const int nxt = tile + gridDim.x;
-    if (nxt < ntiles) {
-      ln_tile(it + 1, xv);  // overlaps the MMA of this tile
-      if (nxt + (int)gridDim.x < ntiles) load_rows(nxt + gridDim.x, xv);  // in flight for a whole tile
       fence_proxy_async_smem();
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * LP_LN_WARPS) : "memory");  // the group's image and tri-bias sums are complete
+      // ---- tri-bias rows of attention row a (warps 2, 3): fp16, log2 domain, 128 x 128 block layout
+      //      [k/8][q][8]; one 16-byte chunk = 8 consecutive keys of one head (padded keys 0); a
+      //      producer-given tri bias: fp16 [B][HEADS][N][N], element (b, hh, a, c) ----
+      if (warp == 2 || warp == 3) {
+        const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+        const int a = args.row_begin + al, c0 = ct * TILE;
+        const float* sB = sBias + (it & 1) * HEADS * TILE;
+        const int t64 = tid - 64, hh = t64 / (TILE / 8), kg = t64 % (TILE / 8);
+        const __half* tbr =
+            tb_given ? static_cast<const __half*>(args.tb_in) + (((size_t)b * HEADS + hh) * N + a) * N : nullptr;
+        auto bias_at = [&](int r0) -> float {
+          if (c0 + r0 >= N) return 0.0f;
+          return (tb_given ? __half2float(tbr[c0 + r0]) : sB[hh * TILE + r0]) * LOG2E;
+        };
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r0 = kg * 8 + 2 * i;
+          w[i] = H16<__half>::pack(bias_at(r0), bias_at(r0 + 1));
+        }
+        *reinterpret_cast<uint4*>(args.ws + args.wl.off_bias + bias16_off(a, c0 + kg * 8, b, hh, args.B, NT)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (tid == 0) mbar_arrive(bar_ready + (it & 1));
     }
-    tri_bias(it, tile);
-    epilogue(it, tile);
-    tc_fence_before();
-    __syncthreads();  // image it + 1 and its tri-bias sums complete; every epilogue done with TMEM
-    tc_fence_after();
-    if (nxt < ntiles) issue_mma(it + 1);
+  } else {
+    // ================================ drain group ================================
+    const int quad = warp & 3;  // TMEM lanes 32 quad..
+    const int e = tid - 32 * LP_LN_WARPS;
+#pragma unroll 1
+    for (int d = 1; d <= LP_PREFETCH; ++d) prefetch_rows(blockIdx.x + d * gridDim.x, e);
+    // TMEM halves this warp drains: [p0, p1)
+    const int p0 = LP_PARTS == 2 ? (warp - LP_LN_WARPS) >> 2 : 0, p1 = LP_PARTS == 2 ? p0 + 1 : 2;
+    int tile = blockIdx.x;
+    for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
+      prefetch_rows(tile + (LP_PREFETCH + 1) * gridDim.x, e);
+      if (warp == LP_LN_WARPS) {
+        if (lane == 0) {
+          mbar_wait(bar_ready + (it & 1), (it >> 1) & 1, status, DEV_TIMEOUT_SYNC);
+          if (it == 0) mbar_wait(bar_w, 0, status, DEV_TIMEOUT_TMA);
+          unsigned char* sAi = sA + (it & 1) * LP_A_BYTES;
+          constexpr uint32_t idesc = make_idesc_f16(128, 256, H16<T>::is_bf16, 0, 0);
+#pragma unroll
+          for (int nh = 0; nh < 2; ++nh) {
+            if (it > 0) mbar_wait(bar_tmem + nh, (it - 1) & 1, status, DEV_TIMEOUT_SYNC);  // half nh of tile it - 1 drained
+            tc_fence_after();
+#pragma unroll
+            for (int ks = 0; ks < C_IN / 16; ++ks) {
+              const uint64_t ad = smem_desc_sw128(smem_u32(sAi) + (ks / 4) * (LP_A_BYTES / 2) + (ks % 4) * 32);
+              const uint64_t bd = smem_desc_noswizzle(smem_u32(sW) + nh * 65536 + ks * 256, 128, 16 * C_IN);
+              umma_ss(tbase + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(bar_mma + nh);
+          }
+          umma_commit(bar_img + (it & 1));
+        }
+        __syncwarp();
+      }
+      const int ct = tile % NT, al = (tile / NT) % R, b = tile / (NT * R);
+      const int c0 = ct * TILE;
+      const int r = quad * 32 + lane, c = c0 + r;
+      const bool valid = c < N;
+#pragma unroll 1
+      for (int part = p0; part < p1; ++part) {  // TMEM half: q|k, v|g
+      mbar_wait(bar_mma + part, it & 1, status, DEV_TIMEOUT_MMA);
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll 1
+      for (int sub = 0; sub < 2; ++sub) {
+        const int tt = 2 * part + sub;  // 0 q, 1 k, 2 v, 3 g
+#pragma unroll 1
+        for (int hh = 0; hh < HEADS; ++hh) {
+          uint32_t acc[32];
+          tmem_ld32(tmem_addr(tbase, quad * 32, tt * 128 + hh * 32), acc);
+          tmem_ld_wait();
+          tmem_regs_ready(acc);
+          if (tt <= 1) {
+            // q (pre-scaled by C^-1/2 log2 e: the core's S is then in log2 units) and k: K-major images
+            const float sc = tt == 0 ? QSCALE_L2 : 1.0f;
+            const float2 sc2 = make_float2(sc, sc);
+            unsigned char* img = args.ws + (tt == 0 ? args.wl.off_q : args.wl.off_k) +
+                                 ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
+            auto qk2 = [&](int i) {
+              const float2 v = __fmul2_rn(make_float2(__uint_as_float(acc[i]), __uint_as_float(acc[i + 1])), sc2);
+              return H16<T>::pack(v.x, v.y);
+            };
+#pragma unroll
+            for (int d = 0; d < C_HEAD; d += 8) {
+              uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+              if (valid) pk = make_uint4(qk2(d), qk2(d + 2), qk2(d + 4), qk2(d + 6));
+              *reinterpret_cast<uint4*>(img + img_off(r, d, C_HEAD)) = pk;
+            }
+          } else if (tt == 2) {
+            // v: fp16 in every 16-bit mode (the P.V product runs in fp16), saturated to the fp16 range,
+            // MN-major image read by the P.V MMA
+            unsigned char* img = args.ws + args.wl.off_v + ((((size_t)b * R + al) * HEADS + hh) * NT + ct) * 8192;
+            // fp16 pair (low half = acc[i]) rounded to nearest and saturated to the finite fp16 range
+            auto sat2 = [&](int i) {
+              uint32_t r;
+              asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "r"(acc[i + 1]), "r"(acc[i]));
+              return r;
+            };
+#pragma unroll
+            for (int d = 0; d < C_HEAD; d += 8) {
+              uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+              if (valid) pk = make_uint4(sat2(d), sat2(d + 2), sat2(d + 4), sat2(d + 6));
+              *reinterpret_cast<uint4*>(img + vimg_off(r, d)) = pk;
+            }
+          } else if (valid) {
+            const float2* gb = reinterpret_cast<const float2*>(sGb + hh * C_HEAD);
+            T* g = reinterpret_cast<T*>(args.ws + args.wl.off_g) + (((size_t)b * R + al) * N + c) * C_IN + hh * C_HEAD;
+            auto g2 = [&](int i) {
+              const float2 v = __fadd2_rn(make_float2(__uint_as_float(acc[i]), __uint_as_float(acc[i + 1])), gb[i / 2]);
+              return H16<T>::pack(v.x, v.y);
+            };
+#pragma unroll
+            for (int d = 0; d < C_HEAD; d += 8)
+              *reinterpret_cast<uint4*>(g + d) = make_uint4(g2(d), g2(d + 2), g2(d + 4), g2(d + 6));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_tmem + part);
+      }
+    }
   }
+  tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);

@@ -134,6 +134,12 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, in
       : "memory");
 }
 
+// Bulk prefetch of [gmem, gmem + bytes) into L2 (16-byte aligned address, size a multiple of 16); no
+// completion to wait for.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gmem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem), "r"(bytes) : "memory");
+}
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
