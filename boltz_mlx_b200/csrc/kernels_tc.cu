@@ -7,8 +7,8 @@
 //                W_qkvg image (512 x 128) -> q (x C^-1/2 log2 e), k, v (fp16) operand images (8 KB per
 //                128-position tile and head), g (row-major 16-bit); tri bias (fp32 SIMT dot from fp32
 //                xn, x log2 e, stored fp16 in 128 x 128 blocks).
-//   core_tc    : per (b, row a, head h, 128-query tile): S = Q K^T (UMMA, SS) in TMEM ->
-//                log2-domain logits fma(S, C^-1/2 log2e, mask bias) + tri bias, online softmax
+//   core_tc    : per (b, row a, head h, 128-query tile): S = Q K^T + tri bias x I (UMMA, SS) in TMEM ->
+//                log2-domain logits (+ mask bias on mixed tiles), online softmax
 //                (fp32) -> P (16-bit) stored to TMEM -> O_part = P V (UMMA, A from TMEM) ->
 //                accumulated in registers; epilogue o / l * sigmoid(g) -> core operand image.
 //   out_proj_tc: y = core W_o^T (UMMA) -> (+ z) -> out, written in z's orientation.
@@ -473,11 +473,14 @@ cudaError_t launch_mask_prep_tc(const LayerArgs& a, cudaStream_t st) {
 //   Each row's leader thread issues that row's work itself: the bulk copies of its Q, K and V tiles
 //   (one slot each, refilled as soon as the MMA that read the slot has completed; after the row's
 //   last tile of an item they are refilled with the first active tile of the row's next item) and
-//   its MMAs (S = Q K^T, then O = P V).  The tri-bias stage is refilled by whichever warp is the
-//   last of the CTA's 8 to finish reading it (an arrival counter in shared memory).
-// TMEM (256 columns): row j owns columns [128 j, 128 j + 128): S (fp32, log2 units) -> x (after the
-// biases) -> P (fp16 pairs in columns 0..63) and the P.V partial (columns 64..111: 32 channels + the
-// row sum from V's ones column).  O is accumulated in registers with a lazy rescale.
+//   its MMAs (S = Q K^T + tri bias, then O = P V).  The tri bias is added on the tensor pipe: the fp16
+//   bias block of the stage, already a K-major operand image, against a 64 x 64 identity, one MMA per
+//   64-key half and K step of 16, accumulating exactly onto S.  The tri-bias stage is refilled by
+//   whichever warp is the last of the CTA's 8 to finish with it (an arrival counter in shared memory).
+// TMEM (256 columns): row j owns columns [128 j, 128 j + 128): S (fp32, log2 units, tri bias included;
+// mixed tiles: + mask bias, written back) -> P (fp16 pairs in columns 0..63) and the P.V partial
+// (columns 64..111: 32 channels + the row sum from V's ones column).  O is accumulated in registers
+// with a lazy rescale.
 // =================================================================================================
 constexpr int CG_RG = 2;            // rows per CTA; two CTAs share an SM
 constexpr int CG_SOFTMAX_WARPS = 4 * CG_RG;
@@ -488,13 +491,14 @@ constexpr int CG_SB = CG_SQ + CG_RG * 8192;        // NB tri-bias stages, 32 KB 
 constexpr int CG_SMB = CG_SB + CG_NB * 32768;      // NB stages x RG mask-bias slices of 512 B
 constexpr int CG_SK = CG_SMB + CG_NB * CG_RG * 512;  // one K slot per row, 8 KB
 constexpr int CG_SV = CG_SK + CG_RG * 8192;        // one V slot per row, 12 KB (8 KB V + 4 KB ones/zeros)
-constexpr int CG_BAR = CG_SV + CG_RG * 12288;
+constexpr int CG_SI = CG_SV + CG_RG * 12288;        // 64 x 64 fp16 identity (K-major image, 8 KB): the tri-bias MMA's B
+constexpr int CG_BAR = CG_SI + 8192;
 constexpr int CG_CLS = CG_BAR + 512;               // 2 (item parity) x RG x 128 key-tile classes
 constexpr int CG_CNT = CG_CLS + 2 * CG_RG * TILE;  // NB tri-bias stage arrival counters
 constexpr int CG_RS = CG_CNT + 16;                 // RG row states (32 B each)
 constexpr int CG_II = CG_RS + CG_RG * 32;          // 3 item-info slots (32 B each)
 constexpr int CG_SMEM = CG_II + 3 * 32;
-static_assert(CG_SMEM <= 232448, "core shared memory");
+static_assert(2 * (CG_SMEM + 1024) <= 233472, "two core CTAs per SM");
 
 // barrier slots
 constexpr int B_BF = 0, B_QF = CG_NB, B_KF = B_QF + CG_RG, B_VF = B_KF + CG_RG, B_SF = B_VF + CG_RG,
@@ -533,14 +537,6 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// x0 + lo(w), x1 + hi(w): fp16 tri bias added to fp32 logits in one mixed-precision add each.
-__device__ __forceinline__ void add_f16_pair(float& x0, float& x1, uint32_t w) {
-  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-      "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
-      : "+f"(x0), "+f"(x1)
-      : "r"(w));
 }
 
 // 2^(x0 - m), 2^(x1 - m) as an fp16 pair (low half x0): one packed fp32 subtract, one conversion to
@@ -655,6 +651,11 @@ __global__ void __launch_bounds__(CG_THREADS, 2) core_tc_kernel(LayerArgs args) 
     uint32_t* tail = reinterpret_cast<uint32_t*>(smem + CG_SV + stg * 12288 + 8192);
     tail[w] = (w < 512 && (w & 3) == 0) ? 0x00003C00u : 0u;  // fp16 1.0 in the low half of each key's first word
   }
+  // identity image: element (n, j) of the K-major no-swizzle layout (LBO 128 B, SBO 1024 B) is fp16 1.0 iff n == j
+  for (int e = tid; e < 4096; e += CG_THREADS) {
+    const int byte = 2 * e, n = (byte >> 10) * 8 + ((byte & 127) >> 4), jj = ((byte & 1023) >> 7) * 8 + ((byte & 15) >> 1);
+    reinterpret_cast<uint16_t*>(smem + CG_SI)[e] = n == jj ? 0x3C00u : 0u;
+  }
   if (tid < CG_RG * 32)
     reinterpret_cast<uint32_t*>(scls)[tid] = class_word(blockIdx.x, tid / 32, tid % 32);
   fence_proxy_async_smem();
@@ -687,6 +688,7 @@ __global__ void __launch_bounds__(CG_THREADS, 2) core_tc_kernel(LayerArgs args) 
   const uint32_t buf0 = tbase + j * 128;  // lane 0 of the row's columns (MMA operands)
   constexpr uint32_t idS = make_idesc_f16(128, 128, H16<T>::is_bf16, 0, 0);
   constexpr uint32_t idPV = make_idesc_f16(128, 48, 0, 0, 1);  // fp16 P (TMEM) x fp16 V (MN-major), N = 32 + 16
+  constexpr uint32_t idB = make_idesc_f16(128, 64, 0, 0, 0);   // fp16 tri bias x fp16 identity, N = 64 keys
   CoreRowState* rs = reinterpret_cast<CoreRowState*>(smem + CG_RS) + j;
   // first active key tile >= kt of row j in the item whose classes are in slot cs
   auto next_active = [&](int cs, int kt) {
@@ -786,14 +788,26 @@ __global__ void __launch_bounds__(CG_THREADS, 2) core_tc_kernel(LayerArgs args) 
       const bool act = cls == 0 || cls == 2;
       float alpha = 1.f;
       if (act && leader) {
-        // S = Q K^T
+        // S = Q K^T + tri bias: the bias block [k/8][q][8] is a K-major fp16 operand (LBO 2048 B, SBO 128 B);
+        // against the 64 x 64 identity it adds bias[q][k] to column k of S exactly, one 64-key half at a time
         mbar_wait(bar + B_KF + j, n & 1, status, DEV_TIMEOUT_TMA);
+        mbar_wait(bar + B_BF + bs, (s / CG_NB) & 1, status, DEV_TIMEOUT_TMA);
         tc_fence_after();
 #pragma unroll
         for (int k2 = 0; k2 < C_HEAD / 16; ++k2) {
           const uint64_t ad = smem_desc_noswizzle(smem_u32(smem + CG_SQ + j * 8192) + k2 * 256, 128, 512);
           const uint64_t bd = smem_desc_noswizzle(smem_u32(smem + CG_SK + j * 8192) + k2 * 256, 128, 512);
           umma_ss(buf0, ad, bd, idS, k2 > 0 ? 1u : 0u);
+        }
+        const uint32_t sbb = smem_u32(smem + CG_SB + bs * 32768), sid = smem_u32(smem + CG_SI);
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const uint64_t ad = smem_desc_noswizzle(sbb + (8 * kh + 2 * k4) * 2048, 2048, 128);
+            const uint64_t bd = smem_desc_noswizzle(sid + 256 * k4, 128, 1024);
+            umma_ss(buf0 + 64 * kh, ad, bd, idB, 1u);
+          }
         }
         umma_commit(bar + B_SF + j);
       }
@@ -811,17 +825,13 @@ __global__ void __launch_bounds__(CG_THREADS, 2) core_tc_kernel(LayerArgs args) 
             load_k(rs->nxt + rs->nxt_first);
           }
         }
-        const unsigned char* tbp = smem + CG_SB + bs * 32768 + t * 16;
         const float* mbp = reinterpret_cast<const float*>(smem + CG_SMB + (bs * CG_RG + j) * 512);
-        // pass 1: x = S (+ mask bias) + tri bias, row max; x written back over S
+        // pass 1: x = S (tri bias included by the MMA) (+ mask bias, written back over S), row max
         float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t sr[32];
           tmem_ld32(buf + 32 * c, sr);
-          uint4 bw[4];
-#pragma unroll
-          for (int gq = 0; gq < 4; ++gq) bw[gq] = *reinterpret_cast<const uint4*>(tbp + (4 * c + gq) * 2048);
           tmem_ld_wait();
           tmem_regs_ready(sr);
           float xs[32];
@@ -835,22 +845,17 @@ __global__ void __launch_bounds__(CG_THREADS, 2) core_tc_kernel(LayerArgs args) 
             }
           }
 #pragma unroll
-          for (int gq = 0; gq < 4; ++gq) {
-            add_f16_pair(xs[8 * gq + 0], xs[8 * gq + 1], bw[gq].x);
-            add_f16_pair(xs[8 * gq + 2], xs[8 * gq + 3], bw[gq].y);
-            add_f16_pair(xs[8 * gq + 4], xs[8 * gq + 5], bw[gq].z);
-            add_f16_pair(xs[8 * gq + 6], xs[8 * gq + 7], bw[gq].w);
-          }
-#pragma unroll
           for (int i = 0; i < 32; i += 8) {
             mxa = max3f(mxa, xs[i], xs[i + 1]);
             mxb = max3f(mxb, xs[i + 2], xs[i + 3]);
             mxc = max3f(mxc, xs[i + 4], xs[i + 5]);
             mxd = max3f(mxd, xs[i + 6], xs[i + 7]);
           }
+          if (cls == 2) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sr[i] = __float_as_uint(xs[i]);
-          tmem_st32(buf + 32 * c, sr);
+            for (int i = 0; i < 32; ++i) sr[i] = __float_as_uint(xs[i]);
+            tmem_st32(buf + 32 * c, sr);
+          }
         }
         tmem_st_wait();
         release_bias(ii, kt);
