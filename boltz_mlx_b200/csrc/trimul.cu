@@ -347,9 +347,19 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       }
     }
   };
+  // the z rows of tile t (128 consecutive pairs: one contiguous 64 KB run) pulled into L2 two tiles ahead
+  // of their register loads, by one thread (the bulk-copy unit takes one request at a time)
+  auto prefetch_tile = [&](long long t) {
+    if (tid == 32 && t < ntiles) {
+      const long long p0 = t * TILE, np = npairs - p0 < TILE ? npairs - p0 : TILE;
+      prefetch_l2_bulk(z + p0 * TM_D, (uint32_t)(np * TM_D * 4));
+    }
+  };
   float4 xv[8];
   long long tile = blockIdx.x;
   if (tile < ntiles) {
+    prefetch_tile(tile + 2 * gridDim.x);
+    prefetch_tile(tile + 3 * gridDim.x);
     load_rows(tile, xv);
     ln_tile(0, xv);
     if (tile + gridDim.x < ntiles) load_rows(tile + gridDim.x, xv);
@@ -359,6 +369,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   }
   for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
     const long long nxt = tile + gridDim.x;
+    prefetch_tile(tile + 4 * gridDim.x);
     if (nxt < ntiles) {
       ln_tile(it + 1, xv);  // overlaps the MMA of this tile
       if (nxt + gridDim.x < ntiles) load_rows(nxt + gridDim.x, xv);
