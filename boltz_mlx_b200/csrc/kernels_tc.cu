@@ -1015,6 +1015,14 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
       bulk_g2s(sA, args.ws + args.wl.off_core + (((size_t)b * R + al) * NT + ct) * 32768, 32768, bars + 0);
       bulk_g2s(sW, args.packed + PackedLayout::img_o, 32768, bars + 0);
     }
+    // the epilogue's residual rows pulled into L2 while the gate and the MMA run, where they are one
+    // contiguous run (a dense view with consecutive pairs as columns)
+    if (tid == 32 && args.add_residual && !args.zv.cblk && args.zv.s_col == C_IN) {
+      const int rows = min(TILE, N - ct * TILE);
+      prefetch_l2_bulk(args.z + b * args.zv.s_batch + (long long)(a - args.zv.row0) * args.zv.s_row +
+                           (long long)ct * TILE * C_IN,
+                       rows * C_IN * 4);
+    }
     // ---- gate: the fp16 core image times sigmoid(g) of the same (b, row, query), rounded once to T, in
     //      place (the MMA then reads a T image); g loads in flight before the image lands ----
     {

@@ -600,6 +600,13 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     mbar_arrive_expect_tx(bars + 0, 32768);
     bulk_g2s(sW, packed + TrimulPacked::img_po, 32768, bars + 0);
   }
+  // the epilogue's row streams (z residual, output gate) pulled into L2 while norm_out and the MMA run:
+  // 128 consecutive pairs are one contiguous run in each
+  if (tid == 32 && p0 < npairs) {
+    const long long np = npairs - p0 < TILE ? npairs - p0 : TILE;
+    if (add_residual) prefetch_l2_bulk(z + p0 * TM_D, (uint32_t)(np * TM_D * 4));
+    prefetch_l2_bulk(gout + p0 * TM_D, (uint32_t)(np * TM_D * sizeof(T)));
+  }
   // ---- norm_out of pair r over channels 64 half .. 64 half + 63 ----
   {
     const int r = tid & (TILE - 1), half = tid >> 7;
