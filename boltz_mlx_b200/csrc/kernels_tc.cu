@@ -539,13 +539,15 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
-// 2^(x0 - m), 2^(x1 - m) as an fp16 pair (low half x0): one packed fp32 subtract, one conversion to
-// an fp16 pair, one packed 16-bit exponential.
+// 2^(x0 - m), 2^(x1 - m) as an fp16 pair (low half x0): one packed fp32 subtract, two fp32 MUFU
+// exponentials, one conversion to an fp16 pair.  The exponent stays fp32 up to the MUFU (a packed
+// 16-bit exponential would round x - m to fp16 first: 2^-7 absolute at |x - m| = 16); the MUFU pipe
+// time is the same (ex2.f16x2 takes two slots) and the core measured 0.7 % faster this way.
 __device__ __forceinline__ uint32_t exp2_pair_f16(float x0, float x1, uint64_t neg_m2) {
   uint32_t r;
-  asm("{\n\t.reg .b64 d;\n\t.reg .f32 a, b;\n\t.reg .b32 t;\n\t"
+  asm("{\n\t.reg .b64 d;\n\t.reg .f32 a, b;\n\t"
       "mov.b64 d, {%1, %2};\n\tadd.rn.f32x2 d, d, %3;\n\tmov.b64 {a, b}, d;\n\t"
-      "cvt.rn.f16x2.f32 t, b, a;\n\tex2.approx.f16x2 %0, t;\n\t}"
+      "ex2.approx.ftz.f32 a, a;\n\tex2.approx.ftz.f32 b, b;\n\tcvt.rn.f16x2.f32 %0, b, a;\n\t}"
       : "=r"(r)
       : "f"(x0), "f"(x1), "l"(neg_m2));
   return r;
