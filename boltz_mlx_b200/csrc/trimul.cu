@@ -43,6 +43,24 @@ __device__ __forceinline__ float tm_warp_sum(float v) {
 }
 
 __device__ __forceinline__ float tm_sigmoid(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// Batch, row and column of pair p of a [B][N][N] grid: 32-bit divides whenever p and N^2 fit in 32 bits
+// (every size whose pair tensor fits in memory), the 64-bit ones otherwise.
+struct PairIdx {
+  long long b, row, col;
+};
+__device__ __forceinline__ PairIdx pair_idx(long long p, int N) {
+  const unsigned long long nn = (unsigned long long)N * (unsigned long long)N;
+  if ((unsigned long long)p < 0x100000000ull && nn < 0x100000000ull) {
+    const uint32_t pu = (uint32_t)p, nu = (uint32_t)nn, bu = pu / nu, pp = pu - bu * nu, ru = pp / (uint32_t)N;
+    return {(long long)bu, (long long)ru, (long long)(pp - ru * (uint32_t)N)};
+  }
+  const long long b = p / (long long)nn, pp = p - b * (long long)nn, r = pp / N;
+  return {b, r, pp - r * N};
+}
+
+// the 16-bit kernels' gate: the approximate divide (2 ulp; 0 once the denominator passes 2^126, where the
+// sigmoid is below 1e-38) in place of the IEEE one, whose refinement costs several instructions a call
+__device__ __forceinline__ float tm_sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // 4 / 2 consecutive elements of type T <-> float
 template <typename T>
@@ -218,7 +236,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   uint64_t* bar_adone = bars + 4;  // every warp has read the a half's columns
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long ntiles = (npairs + TILE - 1) / TILE;
-  const long long nn = (long long)N * N, plane = (long long)N * Np;
+  const long long plane = (long long)N * Np;
   const float* Pf = reinterpret_cast<const float*>(packed);
   if ((smem_u32(sA) & 1023u) != 0) {  // the swizzled image needs a 1024-byte aligned base (CTA-uniform)
     if (tid == 0) atomicCAS(status, 0, (int)DEV_BAD_ALIGN);
@@ -290,8 +308,8 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
     const long long p = tile * TILE + quad * 32 + lane;
     const bool valid = p < npairs;
     const float m = valid ? (mask ? mask[p] : 1.0f) : 0.0f;
-    const long long bb = valid ? p / nn : 0, pp = valid ? p - bb * nn : 0;
-    const long long prow = pp / N, pcol = pp - prow * N;
+    const PairIdx pi = pair_idx(valid ? p : 0, N);
+    const long long bb = pi.b, prow = pi.row, pcol = pi.col;
     // channels 32 tt .. 32 tt + 31 of a (sel 0) or b (sel 1): p at TMEM column colp + c, g at colg + c
     auto gate = [&](int sel, int colp, int colg) {
 #pragma unroll 1
@@ -307,7 +325,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
           T* dst = ab + ((long long)(sel * B + bb) * TM_D + c) * plane + prow * Np + pcol;
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            dst[j * plane] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid(__uint_as_float(gv[j])) * m);
+            dst[j * plane] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid_fast(__uint_as_float(gv[j])) * m);
         }
       }
     };
@@ -701,7 +719,7 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     if (p >= npairs) break;  // warp-uniform
     const float4 y = *reinterpret_cast<const float4*>(stage + r * TT_STAGE_LD + 4 * lane);
     const float4 g = Ew<T>::ld4(gout + p * TM_D + 4 * lane);
-    float4 res = make_float4(y.x * tm_sigmoid(g.x), y.y * tm_sigmoid(g.y), y.z * tm_sigmoid(g.z), y.w * tm_sigmoid(g.w));
+    float4 res = make_float4(y.x * tm_sigmoid_fast(g.x), y.y * tm_sigmoid_fast(g.y), y.z * tm_sigmoid_fast(g.z), y.w * tm_sigmoid_fast(g.w));
     if (add_residual) {
       const float4 zv = reinterpret_cast<const float4*>(z + p * TM_D)[lane];  // out may alias z
       res.x += zv.x; res.y += zv.y; res.z += zv.z; res.w += zv.w;
