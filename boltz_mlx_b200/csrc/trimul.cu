@@ -58,9 +58,21 @@ __device__ __forceinline__ PairIdx pair_idx(long long p, int N) {
   return {b, r, pp - r * N};
 }
 
-// the 16-bit kernels' gate: the approximate divide (2 ulp; 0 once the denominator passes 2^126, where the
-// sigmoid is below 1e-38) in place of the IEEE one, whose refinement costs several instructions a call
-__device__ __forceinline__ float tm_sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// the 16-bit kernels' gate.  fp16 layers: the approximate divide (2 ulp; 0 once the denominator passes
+// 2^126, where the sigmoid is below 1e-38) in place of the IEEE one, whose refinement costs several
+// instructions a call.  bf16 layers: sigmoid(x) = (1 + tanh(x / 2)) / 2 with the one-instruction MUFU
+// tanh (absolute error about 2^-11 in tanh, 2^-12 in the sigmoid: an eighth of bf16's half-ulp at 1/2,
+// so the bf16 rounding of the gated value dominates); one MUFU operation per element instead of two.
+template <typename T>
+__device__ __forceinline__ float tm_sigmoid_fast(float x) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+    return fmaf(0.5f, t, 0.5f);
+  } else {
+    return __fdividef(1.0f, 1.0f + __expf(-x));
+  }
+}
 
 // 4 / 2 consecutive elements of type T <-> float
 template <typename T>
@@ -325,7 +337,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
           T* dst = ab + ((long long)(sel * B + bb) * TM_D + c) * plane + prow * Np + pcol;
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            dst[j * plane] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid_fast(__uint_as_float(gv[j])) * m);
+            dst[j * plane] = static_cast<T>(__uint_as_float(pv[j]) * tm_sigmoid_fast<T>(__uint_as_float(gv[j])) * m);
         }
       }
     };
@@ -719,7 +731,8 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     if (p >= npairs) break;  // warp-uniform
     const float4 y = *reinterpret_cast<const float4*>(stage + r * TT_STAGE_LD + 4 * lane);
     const float4 g = Ew<T>::ld4(gout + p * TM_D + 4 * lane);
-    float4 res = make_float4(y.x * tm_sigmoid_fast(g.x), y.y * tm_sigmoid_fast(g.y), y.z * tm_sigmoid_fast(g.z), y.w * tm_sigmoid_fast(g.w));
+    float4 res = make_float4(y.x * tm_sigmoid_fast<T>(g.x), y.y * tm_sigmoid_fast<T>(g.y), y.z * tm_sigmoid_fast<T>(g.z),
+                             y.w * tm_sigmoid_fast<T>(g.w));
     if (add_residual) {
       const float4 zv = reinterpret_cast<const float4*>(z + p * TM_D)[lane];  // out may alias z
       res.x += zv.x; res.y += zv.y; res.z += zv.z; res.w += zv.w;
