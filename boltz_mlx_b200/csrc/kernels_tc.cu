@@ -1049,7 +1049,18 @@ __global__ void __launch_bounds__(OP_THREADS, 3) out_proj_tc_kernel(LayerArgs ar
         for (int e = 0; e < 4; ++e) {
           const float2 c2 = H16<__half>::unpack(cw[e]);
           const float2 g2 = H16<T>::unpack(gw[e]);
-          ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
+          if constexpr (H16<T>::is_bf16) {
+            // bf16: c sigmoid(g) = c (1 + tanh(g / 2)) / 2 with the one-instruction MUFU tanh (about 2^-12
+            // absolute in the sigmoid, far below bf16's rounding of the product); one MUFU operation
+            // per element instead of two
+            float t0, t1;
+            asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(0.5f * g2.x));
+            asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(0.5f * g2.y));
+            const float hx = 0.5f * c2.x, hy = 0.5f * c2.y;
+            ow[e] = H16<T>::pack(fmaf(hx, t0, hx), fmaf(hy, t1, hy));
+          } else {
+            ow[e] = H16<T>::pack(__fdividef(c2.x, 1.0f + __expf(-g2.x)), __fdividef(c2.y, 1.0f + __expf(-g2.y)));
+          }
         }
         *cp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
