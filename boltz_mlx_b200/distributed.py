@@ -622,14 +622,18 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
             e2e_step(k)
         torch.cuda.synchronize()
         dist.barrier()
-        n_e2e = max(2, min(args.steps, 6))
+        # window: first input copy to last output copy (one pipeline fill included), over enough steps to
+        # keep the fill's share small; the steady-state period between output copies is reported beside it
+        n_e2e = min(max(10, 2 * args.steps), 40)
         t0, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        done = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e)]
         t0.record(s_in)
         for k in range(n_e2e):
             e2e_step(k)
+            done[k].record(s_out)
         t1e.record(s_out)
         torch.cuda.synchronize()
-        e2e = torch.tensor([t0.elapsed_time(t1e) / n_e2e], device=dev)
+        e2e = torch.tensor([t0.elapsed_time(t1e) / n_e2e, done[2].elapsed_time(done[-1]) / (n_e2e - 3)], device=dev)
         dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
         oh = ohs[0]
         status = torch.tensor([_lib.device_status()], device=dev)
@@ -658,10 +662,13 @@ def bench_sharded(args, make_config_inputs, layer_flops, workload_config, metric
                 "exchange": rec["exchange"],
                 "roofline": rec["roofline"],
                 "cpu_baseline": {"note": "timed on rank 0 of the 1-GPU run only (the same host and workload)"},
-                "e2e": {"value": pair_flops / (float(e2e) * 1e-3) / 1e12, "unit": "TFLOP/s",
-                        "ms_per_step": float(e2e), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
+                "e2e": {"value": pair_flops / (float(e2e[0]) * 1e-3) / 1e12, "unit": "TFLOP/s",
+                        "ms_per_step": float(e2e[0]), "h2d_bytes_per_step": (zh.numel() + mh.numel()) * 4 * ws_n,
                         "d2h_bytes_per_step": oh.numel() * 4 * ws_n,
-                        "pipelined": "input copy, pair and output copy of consecutive steps overlap (2 device slots)"},
+                        "pipelined": "input copy, pair and output copy of consecutive steps overlap (2 device slots)",
+                        "steps": n_e2e, "ms_per_step_steady": float(e2e[1]),
+                        "window": "first input copy to last output copy (one pipeline fill included), max over "
+                                  "ranks; ms_per_step_steady = period between consecutive output copies after the fill"},
                 "gpu_launches": rec["gpu_launches"],
                 "device_status": int(status),
                 "clocks": clk.summary(),
