@@ -649,32 +649,42 @@ __global__ void __launch_bounds__(TT_THREADS, 3)
     float v[64];
 #pragma unroll
     for (int d = 0; d < 64; ++d) v[d] = valid ? __ldcs(src + d * plane) : 0.0f;
-    float s0 = 0.f, s1 = 0.f;
+    // statistics and affine on packed fp32 pairs (even, odd channel): the same roundings, in the same
+    // order, as scalar even / odd partial sums, at half the instructions
+    const float2* v2 = reinterpret_cast<const float2*>(v);
+    float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int d = 0; d < 64; d += 2) { s0 += v[d]; s1 += v[d + 1]; }
-    red[half * TILE + r] = s0 + s1;
+    for (int d = 0; d < 32; ++d) s2 = __fadd2_rn(s2, v2[d]);
+    red[half * TILE + r] = s2.x + s2.y;
     __syncthreads();
     const float mean = (red[r] + red[TILE + r]) * (1.0f / TM_D);
-    float q0 = 0.f, q1 = 0.f;
+    const float2 nmean = make_float2(-mean, -mean);
+    float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int d = 0; d < 64; d += 2) {
-      const float e0 = v[d] - mean, e1 = v[d + 1] - mean;
-      q0 += e0 * e0;
-      q1 += e1 * e1;
+    for (int d = 0; d < 32; ++d) {
+      const float2 e = __fadd2_rn(v2[d], nmean);
+      q2 = __ffma2_rn(e, e, q2);
     }
-    red[2 * TILE + half * TILE + r] = q0 + q1;
+    red[2 * TILE + half * TILE + r] = q2.x + q2.y;
     __syncthreads();
     const float var = (red[2 * TILE + r] + red[3 * TILE + r]) * (1.0f / TM_D);
     const float rs = rsqrtf(var + LN_EPS);
-    const float* lw = Pf + TrimulPacked::out_w / 4 + 64 * half;
-    const float* lb = Pf + TrimulPacked::out_b / 4 + 64 * half;
+    const float2 rs2 = make_float2(rs, rs);
+    const float4* lw4 = reinterpret_cast<const float4*>(Pf + TrimulPacked::out_w / 4 + 64 * half);
+    const float4* lb4 = reinterpret_cast<const float4*>(Pf + TrimulPacked::out_b / 4 + 64 * half);
 #pragma unroll
     for (int d = 0; d < 64; d += 8) {
       uint32_t w4[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        w4[e] = H16<T>::pack((v[d + 2 * e] - mean) * rs * __ldg(lw + d + 2 * e) + __ldg(lb + d + 2 * e),
-                             (v[d + 2 * e + 1] - mean) * rs * __ldg(lw + d + 2 * e + 1) + __ldg(lb + d + 2 * e + 1));
+      for (int e = 0; e < 4; e += 2) {
+        const float4 w = __ldg(lw4 + (d + 2 * e) / 4), bq = __ldg(lb4 + (d + 2 * e) / 4);
+        const float2 n0 = __ffma2_rn(__fmul2_rn(__fadd2_rn(v2[(d + 2 * e) / 2], nmean), rs2), make_float2(w.x, w.y),
+                                     make_float2(bq.x, bq.y));
+        const float2 n1 = __ffma2_rn(__fmul2_rn(__fadd2_rn(v2[(d + 2 * e) / 2 + 1], nmean), rs2), make_float2(w.z, w.w),
+                                     make_float2(bq.z, bq.w));
+        w4[e] = H16<T>::pack(n0.x, n0.y);
+        w4[e + 1] = H16<T>::pack(n1.x, n1.y);
+      }
       *reinterpret_cast<uint4*>(sA + img_off(r, 64 * half + d, TM_D)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
     }
   }
